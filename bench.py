@@ -1,0 +1,447 @@
+"""Benchmark of the INT4 super-block batched GEMM hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl moat|reference]
+
+Workload ("Qwen-3B-like FFN"): INT4 super-block weights
+K=3072 x M=8192 quantized from seeded N(0, 0.02), fp16 activations N(0, 1), batch N
+swept over 1, 2, 4, 8, 16, 32. With N GPUs the 8192 columns are column-sharded
+(group-aligned, 8192/N per rank, re-packed bit-identically) and each output
+[N, 8192] is joined with an NCCL all-gather; total work is fixed (strong scaling).
+
+One step = for every batch size in the sweep, the GEMM over each of R distinct copies
+of the weight (a ring far larger than the 126 MB L2, so every weight byte comes from
+HBM), then the all-gather (N > 1 GPUs). ``value`` = algorithmic HBM bytes all ranks
+moved per second (K*M*144/256 + 2*N*K + 2*N*M per call); tokens/s per batch size are
+reported beside it. The GEMM launches of a step are replayed from a CUDA graph.
+
+``e2e`` measures the same sweep through the public Python API (``batched_gemm``) as a
+host user calls it: per call the activations come from pinned host memory and the
+output goes back to pinned host memory, one synchronise per step.
+
+``--impl reference`` times the reference's CPU path (the NumPy oracle port of
+src/dequant.py:116-147 + the fp32 CPU GEMM of test_batched_speed.py:39-42) on this
+host's cores, on a bounded sample of the same workload; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+K_DIM, M_DIM = 3072, 8192
+SWEEP = (1, 2, 4, 8, 16, 32)
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "INT4 GEMM achieved HBM GB/s (3072x8192, N=1..32 sweep)"
+SEED = 2024
+
+
+def gemm_bytes(N, K, M):
+    return K * M * 144 // 256 + 2 * N * K + 2 * N * M
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        return json.load(f)
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = None
+
+    def start(self):
+        try:
+            self.out = open(os.devnull, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=self.out, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            txt, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            txt, _ = self.proc.communicate()
+        rows = []
+        for line in txt.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for nm, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline: the oracle port of the reference's CPU path
+# ---------------------------------------------------------------------------
+class CpuReference:
+    """The reference's CPU path per call: ``unpack_superblock_weights`` (src/dequant.py:116-147)
+    then the fp32 NumPy GEMM (test_batched_speed.py:39-42), via the oracle port.
+    Setup (quantize + pack) happens once, outside any timed region."""
+
+    def __init__(self):
+        from oracle import int4 as O
+        self.O = O
+        self.st = O.quantize_pack_matrix(O.make_weights(K_DIM, M_DIM, SEED))
+        self.xs = {n: O.make_activations(n, K_DIM, n) for n in SWEEP}
+        O.gemm(self.xs[1], O.unpack_superblock_weights(self.st).reshape(K_DIM, M_DIM))  # warm BLAS threads
+
+    def call(self, n):
+        w = self.O.unpack_superblock_weights(self.st).reshape(K_DIM, M_DIM)
+        return self.O.gemm(self.xs[n], w)
+
+    def sweep(self):
+        for n in SWEEP:
+            self.call(n)
+
+    @staticmethod
+    def threads():
+        threads = os.cpu_count()
+        try:
+            from threadpoolctl import threadpool_info
+            threads = max((i.get("num_threads") or 0) for i in threadpool_info()) or threads
+        except Exception:
+            pass
+        return threads
+
+
+def cpu_reference(budget_s=10.0):
+    """CPU baseline: cycle the batch sweep for about ``budget_s`` seconds."""
+    ref = CpuReference()
+    total_bytes, total_tok, calls = 0, 0, 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        for n in SWEEP:
+            ref.call(n)
+            total_bytes += gemm_bytes(n, K_DIM, M_DIM)
+            total_tok += n
+            calls += 1
+    el = time.perf_counter() - t0
+    return {"value": total_bytes / el / 1e9, "unit": "GB/s", "tok_per_s": total_tok / el,
+            "cores": CpuReference.threads(), "kind": "port",
+            "sample": f"{calls} calls ({el:.1f} s) of unpack_superblock_weights + fp32 NumPy GEMM at 3072x8192, "
+                      f"cycling N in {list(SWEEP)}"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    ref = CpuReference()
+    steps = max(1, args.steps)
+    for _ in range(min(args.warmup, 1)):
+        ref.sweep()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ref.sweep()
+    el = time.perf_counter() - t0
+    step_bytes = sum(gemm_bytes(n, K_DIM, M_DIM) for n in SWEEP)
+    value = step_bytes * steps / el / 1e9
+    cores = CpuReference.threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": el / steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16 x int4 -> f32 acc -> f16", "data": "synthetic",
+        "config": {"workload": "BASELINE config 3: INT4 super-block GEMM K=3072 x M=8192, N sweep "
+                               + ",".join(map(str, SWEEP)) + " (host CPU, unsharded)",
+                   "K": K_DIM, "M": M_DIM, "sweep": list(SWEEP)},
+        "tok_per_s": sum(SWEEP) * steps / el,
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{steps} steps x one call per N in {list(SWEEP)} (oracle port of the "
+                                   f"reference CPU path: unpack_superblock_weights + fp32 NumPy GEMM)"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_moat(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from moat_b200 import _lib
+    from moat_b200.dequant import extract_columns, quantize_to_superblocks
+    from moat_b200.dist import column_bounds
+    from moat_b200.gemm import batched_gemm, workspace_bytes
+
+    L = _lib.lib()
+    K, M = K_DIM, M_DIM
+    bounds = column_bounds(M, world, K)
+    c0, c1 = bounds[rank]
+    Ms = c1 - c0
+    sweep = tuple(int(s) for s in args.sweep.split(","))
+
+    # weights: seeded N(0, 0.02) on the device, GPU quantizer, this rank's columns
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED)
+    w = torch.randn((K, M), generator=g, device=dev, dtype=torch.float32) * 0.02
+    full = quantize_to_superblocks(w.reshape(-1))
+    del w
+    shard = extract_columns(full, K, M, c0, c1)
+    del full
+    sb_bytes = shard.numel()
+    R = args.ring
+    if R <= 0:  # ring >= 4x L2 on every rank at up to 8 GPUs: fixed total work
+        R = -(-4 * L2_BYTES * 8 // (K * M * 144 // 256))
+    ring = torch.empty((R, sb_bytes), dtype=torch.uint8, device=dev)
+    ring[:] = shard
+    xs = {n: (torch.randn((n, K), generator=g, device=dev) ).to(torch.float16) for n in sweep}
+    ys = {n: torch.empty((R, n, Ms), dtype=torch.float16, device=dev) for n in sweep}
+    gath = {n: torch.empty((world, R, n, Ms), dtype=torch.float16, device=dev) for n in sweep} if world > 1 else {}
+    yfull = {n: torch.empty((R, n, M), dtype=torch.float16, device=dev) for n in sweep} if world > 1 else {}
+
+    stream = torch.cuda.Stream(device=dev)
+    ws = torch.zeros(max(workspace_bytes(n, K, Ms) for n in sweep), dtype=torch.uint8, device=dev)
+
+    def gemm_launches(n):
+        st = stream.cuda_stream
+        x = xs[n]
+        y = ys[n]
+        for r in range(R):
+            rc = L.mb_int4_gemm(x.data_ptr(), ring[r].data_ptr(), y[r].data_ptr(), n, K, Ms, ws.data_ptr(),
+                                ws.numel(), st)
+            if rc != 0:
+                raise RuntimeError(f"mb_int4_gemm failed: {rc}")
+
+    torch.cuda.synchronize()
+    graphs = {}
+    with torch.cuda.stream(stream):
+        for n in sweep:  # warm the launch path (attributes, occupancy) before capture
+            gemm_launches(n)
+        stream.synchronize()
+        for n in sweep:
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                gemm_launches(n)
+            graphs[n] = gr
+    torch.cuda.synchronize()
+
+    ev = [{n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for n in sweep}
+          for _ in range(args.steps)]
+    gemm_ms = {n: 0.0 for n in sweep}
+
+    def step(record):
+        with torch.cuda.stream(stream):
+            for n in sweep:
+                if record is not None:
+                    ev[record][n][0].record(stream)
+                graphs[n].replay()
+                if record is not None:
+                    ev[record][n][1].record(stream)
+                if world > 1:
+                    dist.all_gather_into_tensor(gath[n].view(-1), ys[n].view(-1))
+                    yfull[n].view(R, n, world, Ms).copy_(gath[n].permute(1, 2, 0, 3))
+
+    for _ in range(args.warmup):
+        step(None)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t_start.record(stream)
+    for i in range(args.steps):
+        step(i)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        for n in sweep:
+            gemm_ms[n] += ev[i][n][0].elapsed_time(ev[i][n][1])
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    elapsed = t_start.elapsed_time(t_end) / 1e3  # seconds
+    el_t = torch.tensor([elapsed], device=dev)
+    if world > 1:
+        dist.all_reduce(el_t, op=dist.ReduceOp.MAX)
+    elapsed = float(el_t.item())
+
+    # per-launch GEMM time (this rank), bytes per launch of this rank's shard
+    per_n = {}
+    tot_bytes_launch, tot_gemm_s = 0, 0.0
+    for n in sweep:
+        t_launch = gemm_ms[n] / 1e3 / (args.steps * R)
+        b = gemm_bytes(n, K, Ms)
+        per_n[str(n)] = {"us_per_call": t_launch * 1e6, "GBps": b / t_launch / 1e9,
+                         "tok_per_s": n * world / max(t_launch, 1e-12) if world == 1 else None}
+        tot_bytes_launch += b * args.steps * R
+        tot_gemm_s += gemm_ms[n] / 1e3
+    achieved = tot_bytes_launch / tot_gemm_s / 1e9
+    step_bytes = sum(gemm_bytes(n, K, Ms) for n in sweep) * R * world
+    value = step_bytes * args.steps / elapsed / 1e9
+    tok_per_s = {str(n): n * R * args.steps / elapsed for n in sweep}
+
+    # e2e through the public API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, dev, stream, shard, sweep, Ms, world, rank, bounds, R)
+
+    peak, peak_kind = load_peaks()
+    traffic = load_traffic()
+    tr = None
+    if traffic and "k_gemm_tma" in traffic:
+        tr = traffic["k_gemm_tma"].get("dram_bytes_per_launch_sweep_avg")
+
+    if rank == 0:
+        cpu = None if (world > 1 or args.no_cpu) else cpu_reference(budget_s=args.cpu_seconds)
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 x int4 -> f32 acc -> f16",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "config": {"workload": "BASELINE config 3: INT4 super-block GEMM K=3072 x M=8192, N sweep "
+                                   + ",".join(map(str, sweep)) + f"; column-sharded over {world} GPU(s)"
+                                   + (" + NCCL all-gather" if world > 1 else ""),
+                       "K": K, "M": M, "sweep": list(sweep), "ring_copies": R,
+                       "ring_bytes_per_rank": R * sb_bytes, "l2": "inputs larger than L2 (weight ring)",
+                       "parallelism": f"column-shard M over {world}"},
+            "tok_per_s": tok_per_s,
+            "per_n": per_n,
+            "roofline": {"bound": "hbm", "kernel": "k_gemm_tma", "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": tr, "bytes_per_launch": "K*M*144/256 + 2NK + 2NM (this rank's shard)"},
+            "gpu_launches": args.steps * R * len(sweep),
+            "clocks": clk,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        graphs.clear()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(args, dev, stream, shard, sweep, Ms, world, rank, bounds, R):
+    """Same sweep through ``moat_b200.gemm.batched_gemm``: per call an H2D of the
+    activations from pinned memory and a D2H of the output into pinned memory."""
+    import torch
+    import torch.distributed as dist
+    from moat_b200.dist import gather_columns
+    from moat_b200.gemm import batched_gemm
+
+    K, M = K_DIM, M_DIM
+    R_e = min(R, args.e2e_ring)
+    ring = [shard.clone() for _ in range(R_e)]
+    g = torch.Generator().manual_seed(SEED + 1)
+    host_x = {n: torch.randn((n, K), generator=g).to(torch.float16).pin_memory() for n in sweep}
+    host_y = {n: torch.empty((R_e, n, M), dtype=torch.float16).pin_memory() for n in sweep}
+    dev_x = {n: torch.empty((n, K), dtype=torch.float16, device=dev) for n in sweep}
+    h2d = sum(n * K * 2 for n in sweep) * R_e
+    d2h = sum(n * M * 2 for n in sweep) * R_e
+
+    def step():
+        with torch.cuda.stream(stream):
+            for n in sweep:
+                for r in range(R_e):
+                    dev_x[n].copy_(host_x[n], non_blocking=True)
+                    y = batched_gemm(dev_x[n], ring[r], K, Ms)
+                    if world > 1:
+                        y = gather_columns(y, bounds)
+                    host_y[n][r].copy_(y, non_blocking=True)
+            stream.synchronize()
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    steps = max(1, args.e2e_steps)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    el = time.perf_counter() - t0
+    el_t = torch.tensor([el], device=dev)
+    if world > 1:
+        dist.all_reduce(el_t, op=dist.ReduceOp.MAX)
+    el = float(el_t.item())
+    step_bytes = sum(gemm_bytes(n, K, Ms) for n in sweep) * R_e * world
+    return {"value": step_bytes * steps / el / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": steps, "calls_per_step": R_e * len(sweep),
+            "tok_per_s": sum(sweep) * R_e * steps / el,
+            "how": "public API batched_gemm per call; pinned H2D of activations and D2H of outputs "
+                   "every call; wall clock around steps, one synchronise per step"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="moat", choices=["moat", "reference"])
+    ap.add_argument("--ring", type=int, default=0, help="weight copies per rank (0: >= 4x L2 at 8 GPUs)")
+    ap.add_argument("--sweep", default=",".join(map(str, SWEEP)))
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--e2e-ring", type=int, default=36)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "moat":
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_moat(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,155 @@
+/*
+ * moat_b200 — C ABI of the B200 (sm_100a) INT4 super-block GEMM and exp-LUT
+ * decode-attention path.
+ *
+ * Conventions (after the reference C ABI, antigravity-engine/src/antigravity_c_api.h):
+ *   - every entry point returns an int32 status: 0 = ok, < 0 = error detected on the
+ *     host before anything was launched (the reference uses -1 for a null / unloaded
+ *     context and -2 for invalid arguments, antigravity_c_api.h:129-130);
+ *   - the caller owns every buffer (antigravity_c_api.h:76-83, 131-143); all pointers
+ *     are DEVICE pointers; nothing here allocates device memory;
+ *   - work is enqueued asynchronously on the caller's stream (`stream` is a
+ *     cudaStream_t; NULL = legacy default stream). The reference is synchronous
+ *     (waitUntilCompleted); callers that need the result on the host synchronise;
+ *   - fp16 data travels as uint16_t bit patterns; the packed weight format is the
+ *     reference's 144-byte super-block (struct SuperBlock, batched_gemm.metal:17-20):
+ *     bytes 0..15 = 8 little-endian fp16 group scales, bytes 16..143 = 128 nibble
+ *     bytes, byte j = element 2j (low nibble) | element 2j+1 (high nibble), each q+8.
+ *     Super-block i holds flat elements [256 i, 256 i + 256) of the row-major [K, M]
+ *     weight, W[k, m] at flat index k*M + m.
+ *   - stateless and thread-safe; kernels that need scratch take a caller-owned
+ *     workspace whose size is given by the matching *_workspace_size() query. A
+ *     workspace must be zero-filled once when allocated; every call leaves it zeroed
+ *     again. One workspace must not be used by two calls that may run concurrently.
+ */
+#ifndef MOAT_B200_H
+#define MOAT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MB_OK 0
+#define MB_ERR_NULL (-1)        /* a required pointer is NULL */
+#define MB_ERR_ARGS (-2)        /* invalid sizes / shapes */
+#define MB_ERR_WORKSPACE (-3)   /* workspace too small */
+#define MB_ERR_LAUNCH (-4)      /* the CUDA launch itself failed */
+#define MB_ERR_ALIGN (-5)       /* a pointer is not 16-byte aligned */
+#define MB_ERR_UNSUPPORTED (-6) /* shape outside what this build supports */
+
+/* Device-side error word bits (read back with mb_int4_gemm_device_status). */
+#define MB_DEVERR_TIMEOUT 1u /* a bounded wait gave up */
+
+#define MB_ABI_VERSION 1
+
+/* ABI version of this library (no reference counterpart; for the ctypes binding). */
+int32_t mb_abi_version(void);
+
+/* Human-readable text for a status code. */
+const char* mb_status_string(int32_t status);
+
+/* ---------------------------------------------------------------------------
+ * INT4 group-32 quantization and super-block packing.
+ * Replaces quantize_weights_int4 (antigravity-engine/src/dequant.py:22-60) when
+ * variant == 0 ("engine": the fp32 scale max|w|/7 is rounded to fp16 first and
+ * the weights are divided by that fp16 scale), and quantize_fp16_to_int4
+ * (src/dequant.py:26-55) when variant == 1 ("top-level": divide by the unrounded
+ * fp32 scale, then store it as fp16). Round half to even, clip to [-8, 7]; a zero
+ * group gets scale 1.0. Also replaces repack_to_superblocks
+ * (antigravity-engine/src/dequant.py:69-132) by writing the 144-byte stream.
+ *   w        n weights, fp32 (w_is_fp16 = 0) or fp16 bit patterns (w_is_fp16 = 1)
+ *   n        multiple of 32; a multiple of 256 if sb_out is given
+ *   q_out    optional int8[n]; scales_out optional fp16[n/32]; sb_out optional
+ *            uint8[n/256*144]. At least one output must be given.
+ * ------------------------------------------------------------------------- */
+int32_t mb_int4_quantize(const void* w, int32_t w_is_fp16, int64_t n, int32_t variant, int8_t* q_out,
+                         uint16_t* scales_out, uint8_t* sb_out, void* stream);
+
+/* Packs int8 q[n] (values in [-8, 7]) and fp16 scales[n/32] into the 144-byte
+ * stream; replaces repack_to_superblocks (antigravity-engine/src/dequant.py:69-132).
+ * n must be a multiple of 256. */
+int32_t mb_int4_pack(const int8_t* q, const uint16_t* scales, int64_t n, uint8_t* sb_out, void* stream);
+
+/* Super-block stream -> int8 q[nsb*256] and fp16 scales[nsb*8]; replaces
+ * unpack_superblock (antigravity-engine/src/dequant.py:135-156). Either output may be NULL. */
+int32_t mb_int4_unpack(const uint8_t* sb, int64_t nsb, int8_t* q_out, uint16_t* scales_out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Dequantization, bit-exact with the reference: out = fp16(q * s), one rounding.
+ * mb_int4_dequant replaces unpack_superblock_weights (src/dequant.py:116-147) and
+ * the Metal dequantize_superblocks_kernel (batched_gemm.metal:41-66): nsb
+ * super-blocks -> fp16[nsb*256].
+ * mb_int4_dequant_q replaces lut_dequantize / arithmetic_dequantize
+ * (antigravity-engine/src/dequant.py:183-252): int8 q[n] with fp16 scales[n/group]
+ * -> fp16[n]; group >= 1, n % group == 0.
+ * ------------------------------------------------------------------------- */
+int32_t mb_int4_dequant(const uint8_t* sb, uint16_t* out, int64_t nsb, void* stream);
+int32_t mb_int4_dequant_q(const int8_t* q, const uint16_t* scales, int64_t n, int32_t group, uint16_t* out,
+                          void* stream);
+
+/* Table gather of lut_dequantize_fp16 (src/dequant.py:79-113): out[i] =
+ * lut[(i / group_len) % lut_rows][clip(idx[i], 0, lut_cols - 1)], fp16.
+ * idx is int32 (already offset the way the reference offsets it). */
+int32_t mb_lut_gather_f16(const int32_t* idx, int64_t n, const uint16_t* lut, int64_t lut_rows, int32_t lut_cols,
+                          int64_t group_len, uint16_t* out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused INT4 super-block batched GEMM: out[N, M] (fp16) = act[N, K] (fp16, row
+ * major) x dequant(sb)[K, M], fp32 accumulation. Replaces the reference's
+ * batched_gemm entry point — Metal batched_gemm_simdgroup (batched_gemm.metal:74-109,
+ * buffers act/weights/out/N/K/M) and fused_batched_gemm_int4 (:116-169), whose CPU
+ * form is the decode step's `activations @ W` (batch_generator.py:290).
+ * Requires K*M % 256 == 0, N >= 1, 16-byte aligned pointers. Any N: rows are
+ * processed in blocks of 32 per launch. The workspace holds fp32 split-K
+ * partial sums, per-strip arrival counters and a device error word.
+ * ------------------------------------------------------------------------- */
+size_t mb_int4_gemm_workspace_size(int32_t N, int32_t K, int32_t M);
+int32_t mb_int4_gemm(const uint16_t* act, const uint8_t* sb, uint16_t* out, int32_t N, int32_t K, int32_t M,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Copies the workspace's device error word (MB_DEVERR_* bits) to *status_out
+ * (host memory) and clears it; synchronises `stream`. No reference counterpart. */
+int32_t mb_int4_gemm_device_status(void* workspace, uint32_t* status_out, void* stream);
+
+/* Columns [c0, c1) of a packed [K, M] weight, re-packed as its own [K, c1-c0]
+ * super-block stream (bit-identical q and scales). Column sharding of M across
+ * GPUs has no reference counterpart (the reference is single-device); the weight
+ * semantics are those of repack_to_superblocks. Needs M % 32 == 0, c0 and c1
+ * multiples of 32, K*(c1-c0) % 256 == 0. */
+int32_t mb_int4_extract_columns(const uint8_t* sb, int32_t K, int32_t M, int32_t c0, int32_t c1, uint8_t* out,
+                                void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Exp-LUT softmax and decode attention.
+ * `table` is the reference's fp16 exp table (ExponentialLUT.lut,
+ * antigravity-engine/src/attention.py:50-51) of `size` entries over [-range_max, 0].
+ * mb_exp_lut_lookup replaces ExponentialLUT.lookup (attention.py:60-85):
+ *   out[i] = table[size-1-trunc(min(|x| / fp32(range_max/(size-1)), size-1))],
+ *   IEEE fp32 divide.
+ * mb_lut_softmax replaces safe_softmax_lut (attention.py:97-134) over the last axis
+ * of x[rows, cols] (fp32): max-subtract, LUT exp, fp32 sum (zero-sum guard), fp16 out.
+ * ------------------------------------------------------------------------- */
+int32_t mb_exp_lut_lookup(const uint16_t* table, int32_t size, float range_max, const float* x, int64_t n,
+                          uint16_t* out, void* stream);
+int32_t mb_lut_softmax(const float* x, int64_t rows, int64_t cols, const uint16_t* table, int32_t size,
+                       float range_max, uint16_t* out, void* stream);
+
+/* Decode attention for one query token per (trace, head), LUT softmax:
+ *   s_l = (q . k_l) * scale (fp32); p = safe_softmax_lut(s) (fp16); out = sum_l p_l v_l.
+ * Composition of gqa_attention_scores_kernel (transformer_ops.metal:94-123),
+ * safe_softmax_lut (attention.py:97-134) and attention_value_kernel
+ * (transformer_ops.metal:186-214). q [T, H, d], k/v [T, H, L, d], out [T, H, d],
+ * all fp16; d % 8 == 0, d <= 256. */
+size_t mb_decode_attn_workspace_size(int32_t T, int32_t H, int32_t L, int32_t d);
+int32_t mb_decode_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int32_t T,
+                       int32_t H, int32_t L, int32_t d, float scale, const uint16_t* table, int32_t size,
+                       float range_max, void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOAT_B200_H */

@@ -1,0 +1,320 @@
+// Exp-LUT softmax and split-KV decode attention for B200 (sm_100a).
+//
+// Reference semantics: ExponentialLUT.lookup / safe_softmax_lut
+// (antigravity-engine/src/attention.py:60-85, 97-134) and the decode attention the
+// reference composes from gqa_attention_scores_kernel (transformer_ops.metal:94-123),
+// the LUT softmax, and attention_value_kernel (transformer_ops.metal:186-214).
+//
+// The LUT index must match the reference bit for bit, so the exponent is never
+// recomputed on the device: idx = trunc(min(|x| / step, size - 1)) with an IEEE
+// fp32 divide (__fdiv_rn) by step = fp32(range_max / (size - 1)), and the value is
+// table[size - 1 - idx]. Because the LUT argument is x - max over the WHOLE row,
+// the attention runs in three streaming passes instead of an online softmax:
+//   1. scores  (streams K): s_l = (q . k_l) * scale -> fp32 workspace, chunk maxima
+//   2. stats   (reads the 4 MB of scores from L2): row max, sum of LUT values
+//   3. p . V   (streams V): p_l = fp16(LUT(s_l - max) / sum), fp32 sum of p_l v_l per
+//      chunk, chunks combined with vector reductions; the last chunk to arrive writes
+//      the fp16 output and re-zeroes the workspace.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace mb {
+
+__device__ __forceinline__ int lut_index(float x, float step, int size) {
+  float f = __fdiv_rn(fabsf(x), step);
+  f = fminf(fmaxf(f, 0.0f), static_cast<float>(size - 1));
+  return static_cast<int>(f);  // truncation toward zero
+}
+
+__device__ __forceinline__ float lut_exp(const uint16_t* __restrict__ table, float x, float step, int size) {
+  return __half2float(__ushort_as_half(__ldg(table + (size - 1 - lut_index(x, step, size)))));
+}
+
+__device__ __forceinline__ float nanmax_f(float a, float b) { return (b > a || b != b) ? b : a; }
+
+template <int BLOCK>
+__device__ __forceinline__ float block_reduce_max(float v, float* sh) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = nanmax_f(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  v = (threadIdx.x < BLOCK / 32) ? sh[threadIdx.x] : -INFINITY;
+  if (w == 0) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = nanmax_f(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (l == 0) sh[0] = v;
+  }
+  __syncthreads();
+  return sh[0];
+}
+
+template <int BLOCK>
+__device__ __forceinline__ float block_reduce_sum(float v, float* sh) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  v = (threadIdx.x < BLOCK / 32) ? sh[threadIdx.x] : 0.0f;
+  if (w == 0) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (l == 0) sh[0] = v;
+  }
+  __syncthreads();
+  return sh[0];
+}
+
+__global__ void __launch_bounds__(256) k_lut_lookup(const uint16_t* __restrict__ table, int size, float step,
+                                                    const float* __restrict__ x, int64_t n, uint16_t* __restrict__ out) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = __ldg(table + (size - 1 - lut_index(x[i], step, size)));
+}
+
+// One CTA per row: max, LUT exp + fp32 sum, normalise to fp16.
+__global__ void __launch_bounds__(256) k_lut_softmax(const float* __restrict__ x, int64_t cols,
+                                                     const uint16_t* __restrict__ table, int size, float step,
+                                                     uint16_t* __restrict__ out) {
+  __shared__ float sh[32];
+  const float* row = x + static_cast<int64_t>(blockIdx.x) * cols;
+  uint16_t* orow = out + static_cast<int64_t>(blockIdx.x) * cols;
+  float m = -INFINITY;
+  for (int64_t c = threadIdx.x; c < cols; c += 256) m = nanmax_f(m, row[c]);
+  m = block_reduce_max<256>(m, sh);
+  float s = 0.0f;
+  for (int64_t c = threadIdx.x; c < cols; c += 256) s += lut_exp(table, row[c] - m, step, size);
+  s = block_reduce_sum<256>(s, sh);
+  if (!(s > 0.0f)) s = 1.0f;  // zero-sum guard (attention.py:131)
+  for (int64_t c = threadIdx.x; c < cols; c += 256)
+    orow[c] = __half_as_ushort(__float2half_rn(__fdiv_rn(lut_exp(table, row[c] - m, step, size), s)));
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention
+// ---------------------------------------------------------------------------
+struct AttnWs {
+  uint32_t* err;
+  uint32_t* counters;  // [T*H]
+  float* stats;        // [T*H][2]: row max, LUT sum
+  float* cmax;         // [T*H][C]
+  float* scores;       // [T*H][L]
+  float* oacc;         // [T*H][d] fp32 partial outputs
+};
+
+constexpr int kAttnBlock = 256;
+
+static inline int attn_chunks(int L) { return std::max(1, std::min(64, (L + 255) / 256)); }
+
+// Pass 1: scores for one (trace, head) and one chunk of the KV length.
+// Each group of d/8 threads handles one key row (16 bytes per thread).
+__global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __restrict__ q,
+                                                            const uint16_t* __restrict__ k, int L, int d, int C,
+                                                            float scale, AttnWs w) {
+  __shared__ float sh[32];
+  const int row = blockIdx.y;  // t*H + h
+  const int chunk = blockIdx.x;
+  const int Lc = (L + C - 1) / C;
+  const int l0 = chunk * Lc, l1 = min(L, l0 + Lc);
+  const int tpr = d / 8;                 // threads per key row
+  const int rows_par = kAttnBlock / tpr; // rows in flight per iteration
+  const int sub = threadIdx.x % tpr, rgrp = threadIdx.x / tpr;
+  const bool active = rgrp < rows_par;
+  float qf[8];
+  {
+    const uint4 qv = *reinterpret_cast<const uint4*>(q + static_cast<int64_t>(row) * d + sub * 8);
+    const __half2* h = reinterpret_cast<const __half2*>(&qv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      qf[2 * i] = f.x;
+      qf[2 * i + 1] = f.y;
+    }
+  }
+  const uint16_t* kb = k + static_cast<int64_t>(row) * L * d;
+  float m = -INFINITY;
+  for (int base = l0; base < l1; base += rows_par) {  // uniform trip count: shuffles below
+    const int l = base + rgrp;
+    float dot = 0.0f;
+    if (active && l < l1) {
+      const uint4 kv = __ldcs(reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(l) * d + sub * 8));
+      const __half2* h = reinterpret_cast<const __half2*>(&kv);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        dot = fmaf(qf[2 * i], f.x, dot);
+        dot = fmaf(qf[2 * i + 1], f.y, dot);
+      }
+    }
+    for (int o = tpr / 2; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    if (active && l < l1 && sub == 0) {
+      const float s = dot * scale;
+      w.scores[static_cast<int64_t>(row) * L + l] = s;
+      m = nanmax_f(m, s);
+    }
+  }
+  m = block_reduce_max<kAttnBlock>(m, sh);
+  if (threadIdx.x == 0) w.cmax[static_cast<int64_t>(row) * C + chunk] = m;
+}
+
+// Pass 2: row max over the chunk maxima, fp32 sum of the LUT values.
+__global__ void __launch_bounds__(kAttnBlock) k_attn_stats(int L, int C, const uint16_t* __restrict__ table, int size,
+                                                           float step, AttnWs w) {
+  __shared__ float sh[32];
+  const int row = blockIdx.x;
+  float m = -INFINITY;
+  for (int c = threadIdx.x; c < C; c += kAttnBlock) m = nanmax_f(m, w.cmax[static_cast<int64_t>(row) * C + c]);
+  m = block_reduce_max<kAttnBlock>(m, sh);
+  const float* s = w.scores + static_cast<int64_t>(row) * L;
+  float acc = 0.0f;
+  for (int l = threadIdx.x; l < L; l += kAttnBlock) acc += lut_exp(table, __ldcg(s + l) - m, step, size);
+  acc = block_reduce_sum<kAttnBlock>(acc, sh);
+  if (threadIdx.x == 0) {
+    w.stats[2 * row] = m;
+    w.stats[2 * row + 1] = (acc > 0.0f) ? acc : 1.0f;
+  }
+}
+
+// Pass 3: out = sum_l fp16(LUT(s_l - m) / sum) * v_l, one chunk per CTA.
+__global__ void __launch_bounds__(kAttnBlock) k_attn_pv(const uint16_t* __restrict__ v, uint16_t* __restrict__ out,
+                                                        int L, int d, int C, const uint16_t* __restrict__ table,
+                                                        int size, float step, AttnWs w) {
+  __shared__ float red[kAttnBlock * 8];
+  __shared__ int is_last;
+  const int row = blockIdx.y, chunk = blockIdx.x;
+  const int Lc = (L + C - 1) / C;
+  const int l0 = chunk * Lc, l1 = min(L, l0 + Lc);
+  const int tpr = d / 8, rows_par = kAttnBlock / tpr;
+  const int sub = threadIdx.x % tpr, rgrp = threadIdx.x / tpr;
+  const bool active = rgrp < rows_par;
+  const float m = w.stats[2 * row], sum = w.stats[2 * row + 1];
+  const float* s = w.scores + static_cast<int64_t>(row) * L;
+  const uint16_t* vb = v + static_cast<int64_t>(row) * L * d;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+  if (active) {
+    for (int l = l0 + rgrp; l < l1; l += rows_par) {
+      const float e = lut_exp(table, __ldcg(s + l) - m, step, size);
+      const float p = __half2float(__float2half_rn(__fdiv_rn(e, sum)));
+      const uint4 vv = __ldcs(reinterpret_cast<const uint4*>(vb + static_cast<int64_t>(l) * d + sub * 8));
+      const __half2* h = reinterpret_cast<const __half2*>(&vv);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        acc[2 * i] = fmaf(p, f.x, acc[2 * i]);
+        acc[2 * i + 1] = fmaf(p, f.y, acc[2 * i + 1]);
+      }
+    }
+  }
+  // reduce across the row groups: red[rgrp][d]
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[threadIdx.x * 8 + i] = active ? acc[i] : 0.0f;  // index = (rgrp*tpr+sub)*8+i
+  __syncthreads();
+  float* oacc = w.oacc + static_cast<int64_t>(row) * d;
+  for (int dd = threadIdx.x; dd < d; dd += kAttnBlock) {
+    float t = 0.0f;
+    for (int g = 0; g < rows_par; ++g) t += red[g * d + dd];
+    atomicAdd(oacc + dd, t);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = (atomicAdd(&w.counters[row], 1u) == static_cast<uint32_t>(C - 1));
+  __syncthreads();
+  if (is_last) {
+    __threadfence();
+    for (int dd = threadIdx.x; dd < d; dd += kAttnBlock) {
+      const float t = __ldcg(oacc + dd);
+      __stcg(oacc + dd, 0.0f);
+      out[static_cast<int64_t>(row) * d + dd] = __half_as_ushort(__float2half_rn(t));
+    }
+    if (threadIdx.x == 0) atomicExch(&w.counters[row], 0u);
+  }
+}
+
+static inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+static AttnWs carve_attn_ws(void* base, int T, int H, int L, int d, int C, size_t* total) {
+  const size_t rows = static_cast<size_t>(T) * H;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  size_t off = 0;
+  AttnWs w;
+  w.err = reinterpret_cast<uint32_t*>(p + off);
+  off += 256;
+  w.counters = reinterpret_cast<uint32_t*>(p + off);
+  off += align256(rows * 4);
+  w.stats = reinterpret_cast<float*>(p + off);
+  off += align256(rows * 8);
+  w.cmax = reinterpret_cast<float*>(p + off);
+  off += align256(rows * C * 4);
+  w.oacc = reinterpret_cast<float*>(p + off);
+  off += align256(rows * d * 4);
+  w.scores = reinterpret_cast<float*>(p + off);
+  off += align256(rows * static_cast<size_t>(L) * 4);
+  if (total) *total = off;
+  return w;
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" {
+
+int32_t mb_exp_lut_lookup(const uint16_t* table, int32_t size, float range_max, const float* x, int64_t n,
+                          uint16_t* out, void* stream) {
+  if (!table || !x || !out) return MB_ERR_NULL;
+  if (size < 2 || !(range_max > 0.0f) || n < 0) return MB_ERR_ARGS;
+  if (n == 0) return MB_OK;
+  const float step = static_cast<float>(static_cast<double>(range_max) / (size - 1));
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 32);
+  k_lut_lookup<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(table, size, step, x, n, out);
+  return launch_status();
+}
+
+int32_t mb_lut_softmax(const float* x, int64_t rows, int64_t cols, const uint16_t* table, int32_t size,
+                       float range_max, uint16_t* out, void* stream) {
+  if (!x || !table || !out) return MB_ERR_NULL;
+  if (rows < 0 || cols < 1 || size < 2 || !(range_max > 0.0f) || rows > 2147483647LL) return MB_ERR_ARGS;
+  if (rows == 0) return MB_OK;
+  const float step = static_cast<float>(static_cast<double>(range_max) / (size - 1));
+  k_lut_softmax<<<static_cast<unsigned>(rows), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, cols, table, size,
+                                                                                           step, out);
+  return launch_status();
+}
+
+size_t mb_decode_attn_workspace_size(int32_t T, int32_t H, int32_t L, int32_t d) {
+  if (T < 1 || H < 1 || L < 1 || d < 1) return 0;
+  size_t total = 0;
+  carve_attn_ws(nullptr, T, H, L, d, attn_chunks(L), &total);
+  return total;
+}
+
+int32_t mb_decode_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int32_t T, int32_t H,
+                       int32_t L, int32_t d, float scale, const uint16_t* table, int32_t size, float range_max,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !out || !table || !workspace) return MB_ERR_NULL;
+  if (T < 1 || H < 1 || L < 1 || d < 8 || d > 256 || d % 8 != 0 || (d & (d - 1)) != 0 || size < 2 ||
+      !(range_max > 0.0f))
+    return MB_ERR_ARGS;
+  if (static_cast<int64_t>(T) * H > 65535) return MB_ERR_UNSUPPORTED;
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(workspace, 256)) return MB_ERR_ALIGN;
+  if (workspace_bytes < mb_decode_attn_workspace_size(T, H, L, d)) return MB_ERR_WORKSPACE;
+  const int C = attn_chunks(L);
+  AttnWs w = carve_attn_ws(workspace, T, H, L, d, C, nullptr);
+  const float step = static_cast<float>(static_cast<double>(range_max) / (size - 1));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rows = T * H;
+  k_attn_scores<<<dim3(C, rows), kAttnBlock, 0, st>>>(q, k, L, d, C, scale, w);
+  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
+  k_attn_stats<<<rows, kAttnBlock, 0, st>>>(L, C, table, size, step, w);
+  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
+  k_attn_pv<<<dim3(C, rows), kAttnBlock, 0, st>>>(v, out, L, d, C, table, size, step, w);
+  return launch_status();
+}
+
+}  // extern "C"

@@ -1,0 +1,86 @@
+"""The ``batched_gemm`` entry point: N decode traces x INT4 super-block weights.
+
+``out[N, M] = activations[N, K] @ dequant(superblocks)[K, M]`` in fp16 with fp32
+accumulation, computed by the fused weight-streaming sm_100a kernel (C ABI
+``mb_int4_gemm``). Replaces the reference's Metal ``batched_gemm_simdgroup`` /
+``fused_batched_gemm_int4`` (``antigravity-engine/src/shaders/batched_gemm.metal:74-169``,
+buffers ``activations, weights, output, N, K, M``) whose CPU form is the decode
+step's ``activations @ W`` (``antigravity-engine/src/batch_generator.py:290``).
+
+The weights are the reference's 144-byte super-block stream of the row-major
+``[K, M]`` matrix (flat index ``k*M + m``). Host (NumPy) inputs are copied to the
+GPU and the result copied back, which is the end-to-end path; torch CUDA tensors stay
+on the device.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import _lib
+from ._lib import check, lib, ptr, stream_of, to_device
+
+_pool = _lib.WorkspacePool()
+
+
+def workspace_bytes(N: int, K: int, M: int) -> int:
+    return int(lib().mb_int4_gemm_workspace_size(N, K, M))
+
+
+def batched_gemm(activations, superblocks, K: int, M: int, out=None):
+    """fp16 ``[N, K] x int4[K, M] -> fp16 [N, M]`` with fp32 accumulation.
+
+    activations: fp16 ``[N, K]`` (NumPy or torch CUDA); superblocks: uint8
+    ``[K*M/256*144]`` super-block stream on the same device (or NumPy); ``out``:
+    optional fp16 ``[N, M]`` CUDA tensor to write into.
+    """
+    t = _lib.torch()
+    a, was_np = to_device(activations, t.float16)
+    if a.dim() == 1:
+        a = a.reshape(1, -1)
+    N = a.shape[0]
+    if a.shape[1] != K:
+        raise ValueError(f"activations have {a.shape[1]} columns, expected K={K}")
+    if (K * M) % 256 != 0:
+        raise ValueError(f"K*M = {K * M} is not a multiple of 256")
+    sb, _ = to_device(superblocks, t.uint8, a.device)
+    if sb.numel() != K * M // 256 * 144:
+        raise ValueError(f"superblock stream has {sb.numel()} bytes, expected {K * M // 256 * 144}")
+    if out is None:
+        out = t.empty((N, M), dtype=t.float16, device=a.device)
+    elif out.shape != (N, M) or out.dtype != t.float16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous fp16 [N, M] tensor")
+    st = stream_of(a.device)
+    nbytes = workspace_bytes(N, K, M)
+    ws = _pool.get(a.device, st, nbytes)
+    check(lib().mb_int4_gemm(ptr(a), ptr(sb), ptr(out), N, K, M, ptr(ws), ws.numel(), st), "mb_int4_gemm")
+    if was_np:
+        return out.cpu().numpy()
+    return out
+
+
+def device_status(device=None) -> int:
+    """Read and clear the device error word of this stream's GEMM workspace
+    (non-zero means a bounded wait inside the kernel gave up)."""
+    import ctypes
+    t = _lib.torch()
+    dev = device or t.device("cuda", t.cuda.current_device())
+    st = stream_of(dev)
+    ws = _pool.get(dev, st, 256)
+    v = ctypes.c_uint32(0)
+    check(lib().mb_int4_gemm_device_status(ptr(ws), ctypes.byref(v), st), "mb_int4_gemm_device_status")
+    return int(v.value)
+
+
+def gemm_bytes(N: int, K: int, M: int) -> int:
+    """Algorithmic HBM bytes of one call: packed weights + activations + output."""
+    return K * M * 144 // 256 + 2 * N * K + 2 * N * M
+
+
+def gemm_flops(N: int, K: int, M: int) -> int:
+    return 2 * N * K * M
+
+
+__all__ = ["batched_gemm", "workspace_bytes", "device_status", "gemm_bytes", "gemm_flops"]
+
+_ = np  # numpy inputs are accepted through to_device

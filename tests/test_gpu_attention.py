@@ -1,0 +1,100 @@
+"""GPU parity of the exp-LUT lookup, LUT softmax and LUT decode attention.
+
+LUT lookups are bit-exact (same index rule, same table). The softmax's fp32 sum may
+be ordered differently from NumPy's pairwise sum, so probabilities are held to 2
+fp16 ulps; attention outputs to the north-star 1e-2 relative bar plus a relative L2
+error <= 1e-3 against the reference composition.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import attention as OA
+
+pytestmark = pytest.mark.gpu
+
+
+def test_exp_table_is_reference_table(golden_meta):
+    import hashlib
+    from moat_b200.attention import ExponentialLUT
+    for r in (10, 16):
+        t = ExponentialLUT(range_max=float(r)).lut
+        assert hashlib.sha256(t.tobytes()).hexdigest() == golden_meta[f"exp_table_r{r}_sha256"]
+
+
+@pytest.mark.parametrize("r", [10, 16])
+def test_lookup_bit_exact(cuda, golden, r):
+    from moat_b200.attention import ExponentialLUT
+    e = ExponentialLUT(range_max=float(r))
+    got = e.lookup(golden[f"lookup_in_r{r}"])
+    np.testing.assert_array_equal(got.view(np.uint16), golden[f"lookup_out_r{r}"].view(np.uint16))
+
+
+@pytest.mark.parametrize("name", ["s4x16", "s32x128", "s8x4096", "s3x7", "s2x1"])
+def test_lut_softmax_matches_reference(cuda, golden, name):
+    from moat_b200.attention import ExponentialLUT, safe_softmax_lut
+    e = ExponentialLUT()
+    got = safe_softmax_lut(golden[f"sm_in_{name}"], e).astype(np.float32)
+    ref = golden[f"sm_out_{name}"]
+    ulp = np.spacing(ref.astype(np.float16)).astype(np.float32)
+    assert np.all(np.abs(got - ref.astype(np.float32)) <= 2 * ulp)
+
+
+def test_softmax_axis_and_edges(cuda):
+    from moat_b200.attention import ExponentialLUT, safe_softmax_lut
+    e = ExponentialLUT()
+    x = np.random.default_rng(0).standard_normal((5, 7, 9)).astype(np.float32)
+    t = OA.exp_table()
+    for ax in (0, 1, 2, -1):
+        got = safe_softmax_lut(x, e, axis=ax).astype(np.float32)
+        ref = OA.safe_softmax_lut(x, t, 10.0, axis=ax).astype(np.float32)
+        np.testing.assert_allclose(got, ref, atol=2e-3)
+    big = np.array([[1000.0, 999.0, 998.0]], np.float16)
+    assert np.isclose(safe_softmax_lut(big, e).astype(np.float32).sum(), 1.0, atol=1e-2)
+    one = safe_softmax_lut(np.array([[42.0]], np.float16), e)
+    assert float(one[0, 0]) == 1.0
+
+
+def test_attention_reduced_config4_golden(cuda, golden, golden_meta):
+    from moat_b200.attention import ExponentialLUT, decode_attention
+    a = golden_meta["attn"]
+    q, k, v = OA.make_attention_inputs(a["T"], a["H"], a["L"], a["d"], a["seed"])
+    e = ExponentialLUT(range_max=a["range_max"])
+    got = decode_attention(q, k, v, e).astype(np.float32)
+    ref = golden["attn_out"].astype(np.float32)
+    np.testing.assert_allclose(got, ref, rtol=1e-2, atol=1e-2)
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-3
+
+
+@pytest.mark.parametrize("T,H,L,d", [(1, 1, 1, 128), (2, 3, 77, 64), (1, 2, 4097, 128), (3, 1, 300, 256),
+                                     (2, 2, 1000, 8)])
+def test_attention_ragged(cuda, T, H, L, d):
+    from moat_b200.attention import ExponentialLUT, decode_attention
+    q, k, v = OA.make_attention_inputs(T, H, L, d, L + d)
+    e = ExponentialLUT(range_max=16.0)
+    got = decode_attention(q, k, v, e).astype(np.float32)
+    ref = OA.decode_attention(q, k, v, e.lut, 16.0).astype(np.float32)
+    np.testing.assert_allclose(got, ref, rtol=1e-2, atol=1e-2)
+
+
+def test_attention_full_config4_vs_exact(cuda):
+    """BASELINE config 4 at full size (16 traces x 16 heads x L=4096 x d=128): the
+    LUT attention stays within 1e-2 of exact-exp attention, and repeated calls
+    agree (workspace re-zeroed)."""
+    import torch
+    from moat_b200.attention import ExponentialLUT, decode_attention
+    T, H, L, d = 16, 16, 4096, 128
+    q, k, v = OA.make_attention_inputs(T, H, L, d, 4)
+    qd, kd, vd = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    e = ExponentialLUT(range_max=16.0)
+    out1 = decode_attention(qd, kd, vd, e).float()
+    out2 = decode_attention(qd, kd, vd, e).float()
+    assert torch.equal(out1, out2)
+    s = torch.einsum("thd,thld->thl", qd.float(), kd.float()) / np.sqrt(d)
+    exact = torch.einsum("thl,thld->thd", torch.softmax(s, -1), vd.float())
+    rel = (out1 - exact).norm() / exact.norm()
+    assert rel.item() < 1e-2
+    # the reference composition on two (trace, head) rows, computed on the CPU oracle
+    tbl = e.lut
+    ref = OA.decode_attention(q[:2, :2], k[:2, :2], v[:2, :2], tbl, 16.0).astype(np.float32)
+    np.testing.assert_allclose(out1[:2, :2].cpu().numpy(), ref, rtol=1e-2, atol=1e-2)
