@@ -218,7 +218,7 @@ def run_moat(args):
     from moat_b200 import _lib
     from moat_b200.dequant import extract_columns, quantize_to_superblocks
     from moat_b200.dist import column_bounds
-    from moat_b200.gemm import batched_gemm, workspace_bytes
+    from moat_b200.gemm import plan
 
     L = _lib.lib()
     K, M = K_DIM, M_DIM
@@ -247,15 +247,14 @@ def run_moat(args):
     yfull = {n: torch.empty((R, n, M), dtype=torch.float16, device=dev) for n in sweep} if world > 1 else {}
 
     stream = torch.cuda.Stream(device=dev)
-    ws = torch.zeros(max(workspace_bytes(n, K, Ms) for n in sweep), dtype=torch.uint8, device=dev)
+    plans = {n: plan(n, K, Ms) for n in sweep}
 
     def gemm_launches(n):
         st = stream.cuda_stream
         x = xs[n]
         y = ys[n]
         for r in range(R):
-            rc = L.mb_int4_gemm(x.data_ptr(), ring[r].data_ptr(), y[r].data_ptr(), n, K, Ms, ws.data_ptr(),
-                                ws.numel(), st)
+            rc = L.mb_int4_gemm(x.data_ptr(), ring[r].data_ptr(), y[r].data_ptr(), n, K, Ms, None, st)
             if rc != 0:
                 raise RuntimeError(f"mb_int4_gemm failed: {rc}")
 
@@ -356,6 +355,7 @@ def run_moat(args):
                        "parallelism": f"column-shard M over {world}"},
             "tok_per_s": tok_per_s,
             "per_n": per_n,
+            "plans": {str(n): plans[n] for n in sweep},
             "roofline": {"bound": "hbm", "kernel": "k_gemm_tma", "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": tr, "bytes_per_launch": "K*M*144/256 + 2NK + 2NM (this rank's shard)"},

@@ -17,10 +17,10 @@
  *     bytes, byte j = element 2j (low nibble) | element 2j+1 (high nibble), each q+8.
  *     Super-block i holds flat elements [256 i, 256 i + 256) of the row-major [K, M]
  *     weight, W[k, m] at flat index k*M + m.
- *   - stateless and thread-safe; kernels that need scratch take a caller-owned
- *     workspace whose size is given by the matching *_workspace_size() query. A
- *     workspace must be zero-filled once when allocated; every call leaves it zeroed
- *     again. One workspace must not be used by two calls that may run concurrently.
+ *   - stateless and thread-safe; a kernel that needs scratch (decode attention)
+ *     takes a caller-owned workspace whose size is given by the matching
+ *     *_workspace_size() query; it needs no initial contents, but one workspace
+ *     must not be used by two calls that may run concurrently.
  */
 #ifndef MOAT_B200_H
 #define MOAT_B200_H
@@ -40,7 +40,7 @@ extern "C" {
 #define MB_ERR_ALIGN (-5)       /* a pointer is not 16-byte aligned */
 #define MB_ERR_UNSUPPORTED (-6) /* shape outside what this build supports */
 
-/* Device-side error word bits (read back with mb_int4_gemm_device_status). */
+/* Device-side error word bits (written to a caller-provided device word). */
 #define MB_DEVERR_TIMEOUT 1u /* a bounded wait gave up */
 
 #define MB_ABI_VERSION 1
@@ -102,17 +102,20 @@ int32_t mb_lut_gather_f16(const int32_t* idx, int64_t n, const uint16_t* lut, in
  * batched_gemm entry point — Metal batched_gemm_simdgroup (batched_gemm.metal:74-109,
  * buffers act/weights/out/N/K/M) and fused_batched_gemm_int4 (:116-169), whose CPU
  * form is the decode step's `activations @ W` (batch_generator.py:290).
- * Requires K*M % 256 == 0, N >= 1, 16-byte aligned pointers. Any N: rows are
- * processed in blocks of 32 per launch. The workspace holds fp32 split-K
- * partial sums, per-strip arrival counters and a device error word.
+ * Requires K*M % 256 == 0 and N >= 1; any N (rows are processed in blocks of 32
+ * per launch). No scratch memory: split-K partial sums are reduced on chip.
+ * dev_err is an optional DEVICE word (may be NULL) that receives MB_DEVERR_* bits
+ * if a bounded wait inside the kernel gives up. The fast path needs K % 8 == 0,
+ * M % 128 == 0 and 16-byte aligned act / sb; other shapes take a slower path.
  * ------------------------------------------------------------------------- */
-size_t mb_int4_gemm_workspace_size(int32_t N, int32_t K, int32_t M);
 int32_t mb_int4_gemm(const uint16_t* act, const uint8_t* sb, uint16_t* out, int32_t N, int32_t K, int32_t M,
-                     void* workspace, size_t workspace_bytes, void* stream);
+                     uint32_t* dev_err, void* stream);
 
-/* Copies the workspace's device error word (MB_DEVERR_* bits) to *status_out
- * (host memory) and clears it; synchronises `stream`. No reference counterpart. */
-int32_t mb_int4_gemm_device_status(void* workspace, uint32_t* status_out, void* stream);
+/* Launch plan the GEMM would use for a shape (introspection, no reference
+ * counterpart): info[0] fast path (1/0), [1] strip width, [2] CTAs per cluster
+ * (K split), [3] grid size, [4] pipeline stages, [5] dynamic shared memory bytes,
+ * [6] row phases, [7] 8-row batch tiles. info must hold 8 int32. */
+int32_t mb_int4_gemm_plan(int32_t N, int32_t K, int32_t M, int32_t* info);
 
 /* Columns [c0, c1) of a packed [K, M] weight, re-packed as its own [K, c1-c0]
  * super-block stream (bit-identical q and scales). Column sharding of M across
@@ -142,7 +145,8 @@ int32_t mb_lut_softmax(const float* x, int64_t rows, int64_t cols, const uint16_
  * Composition of gqa_attention_scores_kernel (transformer_ops.metal:94-123),
  * safe_softmax_lut (attention.py:97-134) and attention_value_kernel
  * (transformer_ops.metal:186-214). q [T, H, d], k/v [T, H, L, d], out [T, H, d],
- * all fp16; d % 8 == 0, d <= 256. */
+ * all fp16; d a power of two in [8, 256]. The workspace needs no initialisation
+ * (the kernels overwrite every byte they read). */
 size_t mb_decode_attn_workspace_size(int32_t T, int32_t H, int32_t L, int32_t d);
 int32_t mb_decode_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int32_t T,
                        int32_t H, int32_t L, int32_t d, float scale, const uint16_t* table, int32_t size,

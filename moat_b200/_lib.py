@@ -27,9 +27,8 @@ SIGNATURES = {
     "mb_int4_dequant": (_c_i32, [_vp, _vp, _c_i64, _vp]),
     "mb_int4_dequant_q": (_c_i32, [_vp, _vp, _c_i64, _c_i32, _vp, _vp]),
     "mb_lut_gather_f16": (_c_i32, [_vp, _c_i64, _vp, _c_i64, _c_i32, _c_i64, _vp, _vp]),
-    "mb_int4_gemm_workspace_size": (_c_sz, [_c_i32, _c_i32, _c_i32]),
-    "mb_int4_gemm": (_c_i32, [_vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _vp, _c_sz, _vp]),
-    "mb_int4_gemm_device_status": (_c_i32, [_vp, ctypes.POINTER(ctypes.c_uint32), _vp]),
+    "mb_int4_gemm": (_c_i32, [_vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _vp, _vp]),
+    "mb_int4_gemm_plan": (_c_i32, [_c_i32, _c_i32, _c_i32, ctypes.POINTER(_c_i32)]),
     "mb_int4_extract_columns": (_c_i32, [_vp, _c_i32, _c_i32, _c_i32, _c_i32, _vp, _vp]),
     "mb_exp_lut_lookup": (_c_i32, [_vp, _c_i32, _c_f, _vp, _c_i64, _vp, _vp]),
     "mb_lut_softmax": (_c_i32, [_vp, _c_i64, _c_i64, _vp, _c_i32, _c_f, _vp, _vp]),

@@ -13,8 +13,9 @@
 //   1. scores  (streams K): s_l = (q . k_l) * scale -> fp32 workspace, chunk maxima
 //   2. stats   (reads the 4 MB of scores from L2): row max, sum of LUT values
 //   3. p . V   (streams V): p_l = fp16(LUT(s_l - max) / sum), fp32 sum of p_l v_l per
-//      chunk, chunks combined with vector reductions; the last chunk to arrive writes
-//      the fp16 output and re-zeroes the workspace.
+//      chunk into a per-chunk slot; the last chunk to arrive sums the slots in chunk
+//      order (deterministic) and writes the fp16 output. The workspace needs no
+//      initial contents (pass 1 resets the arrival counters).
 #include <algorithm>
 
 #include "common.cuh"
@@ -103,7 +104,7 @@ struct AttnWs {
   float* stats;        // [T*H][2]: row max, LUT sum
   float* cmax;         // [T*H][C]
   float* scores;       // [T*H][L]
-  float* oacc;         // [T*H][d] fp32 partial outputs
+  float* part;         // [T*H][C][d] fp32 per-chunk partial outputs
 };
 
 constexpr int kAttnBlock = 256;
@@ -135,6 +136,7 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __re
       qf[2 * i + 1] = f.y;
     }
   }
+  if (chunk == 0 && threadIdx.x == 0) w.counters[row] = 0u;  // pass 3's arrival counter
   const uint16_t* kb = k + static_cast<int64_t>(row) * L * d;
   float m = -INFINITY;
   for (int base = l0; base < l1; base += rows_par) {  // uniform trip count: shuffles below
@@ -211,28 +213,27 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_pv(const uint16_t* __restri
       }
     }
   }
-  // reduce across the row groups: red[rgrp][d]
+  // reduce across the row groups (fixed order): red[rgrp][d]
 #pragma unroll
   for (int i = 0; i < 8; ++i) red[threadIdx.x * 8 + i] = active ? acc[i] : 0.0f;  // index = (rgrp*tpr+sub)*8+i
   __syncthreads();
-  float* oacc = w.oacc + static_cast<int64_t>(row) * d;
+  float* part = w.part + static_cast<int64_t>(row) * C * d;
   for (int dd = threadIdx.x; dd < d; dd += kAttnBlock) {
     float t = 0.0f;
     for (int g = 0; g < rows_par; ++g) t += red[g * d + dd];
-    atomicAdd(oacc + dd, t);
+    __stcg(part + static_cast<int64_t>(chunk) * d + dd, t);
   }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) is_last = (atomicAdd(&w.counters[row], 1u) == static_cast<uint32_t>(C - 1));
   __syncthreads();
-  if (is_last) {
+  if (is_last) {  // the last chunk sums all chunks in chunk order: deterministic
     __threadfence();
     for (int dd = threadIdx.x; dd < d; dd += kAttnBlock) {
-      const float t = __ldcg(oacc + dd);
-      __stcg(oacc + dd, 0.0f);
+      float t = 0.0f;
+      for (int c = 0; c < C; ++c) t += __ldcg(part + static_cast<int64_t>(c) * d + dd);
       out[static_cast<int64_t>(row) * d + dd] = __half_as_ushort(__float2half_rn(t));
     }
-    if (threadIdx.x == 0) atomicExch(&w.counters[row], 0u);
   }
 }
 
@@ -251,8 +252,8 @@ static AttnWs carve_attn_ws(void* base, int T, int H, int L, int d, int C, size_
   off += align256(rows * 8);
   w.cmax = reinterpret_cast<float*>(p + off);
   off += align256(rows * C * 4);
-  w.oacc = reinterpret_cast<float*>(p + off);
-  off += align256(rows * d * 4);
+  w.part = reinterpret_cast<float*>(p + off);
+  off += align256(rows * C * d * 4);
   w.scores = reinterpret_cast<float*>(p + off);
   off += align256(rows * static_cast<size_t>(L) * 4);
   if (total) *total = off;
@@ -267,9 +268,9 @@ extern "C" {
 
 int32_t mb_exp_lut_lookup(const uint16_t* table, int32_t size, float range_max, const float* x, int64_t n,
                           uint16_t* out, void* stream) {
-  if (!table || !x || !out) return MB_ERR_NULL;
   if (size < 2 || !(range_max > 0.0f) || n < 0) return MB_ERR_ARGS;
   if (n == 0) return MB_OK;
+  if (!table || !x || !out) return MB_ERR_NULL;
   const float step = static_cast<float>(static_cast<double>(range_max) / (size - 1));
   const int64_t blocks = std::min<int64_t>((n + 255) / 256, static_cast<int64_t>(sm_count()) * 32);
   k_lut_lookup<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(table, size, step, x, n, out);

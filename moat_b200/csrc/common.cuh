@@ -26,6 +26,11 @@ inline int launch_status() {
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Encode a 3-D tiled uint8 tensor map (dims inner -> outer, strides of dims 1 and 2 in
+// bytes). Returns false if the driver rejects the parameters.
+bool encode_tmap_3d_u8(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
+                       const uint32_t box[3]);
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
@@ -164,6 +169,45 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
 
 __device__ __forceinline__ void red_add_v2(float* addr, float a, float b) {
   asm volatile("red.relaxed.gpu.global.add.v2.f32 [%0], {%1, %2};" ::"l"(addr), "f"(a), "f"(b) : "memory");
+}
+
+
+// ---------------------------------------------------------------------------
+// Thread-block cluster helpers (distributed shared memory)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Full cluster barrier: every thread of every CTA in the cluster arrives (release)
+// and waits (acquire), so shared-memory writes before it are visible cluster-wide.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory location in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// 3-D tiled TMA load (global -> this CTA's shared memory), completion on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
+      : "memory");
 }
 
 }  // namespace mb

@@ -6,87 +6,82 @@
 // CPU form `activations @ W`, batch_generator.py:290). The weight stream is the
 // reference's 144-byte super-block format, read in place.
 //
-// Design (weight-streaming, HBM bound):
-//  * Work = (strip of 256 columns = one super-block per row) x (16-row k slices),
-//    split evenly over a persistent grid in strip-major order (stream-K), so every
-//    SM streams the same number of weight bytes whatever K, M and the SM count are.
-//  * One producer thread per CTA issues 2-D TMA tile loads (cp.async.bulk.tensor):
-//    16 rows x 144 B of super-blocks per slice (L2 evict-first) and a 64-wide k tile
-//    of the activations (128-byte swizzle, L2 evict-last) into a multi-stage
-//    shared-memory ring guarded by mbarriers.
-//  * Programmatic dependent launch: weights never depend on the previous kernel, so
-//    the producer prefetches its first stages BEFORE griddepcontrol.wait; only the
-//    activation loads and all global writes wait for the previous grid.
-//  * Four consumer warps expand nibbles straight into mma.m16n8k16 A fragments in
-//    registers (byte permute + magic-exponent fp16 conversion + one fp16 multiply by
-//    the group scale, bit-exact with the reference dequant) and accumulate in fp32.
-//    The batch (padded to 8/16/32 rows) is the MMA n dimension.
-//  * Split-K partial sums go to an fp32 workspace in L2 with vector reductions; the
-//    last CTA to finish a strip (arrival counter) converts it to fp16 and re-zeroes
-//    the workspace, so the workspace is clean for the next call.
+// Design (weight streaming, HBM bound):
+//  * The M columns are cut into strips of WS = 256 (one super-block per row) or 128
+//    columns. Each strip is handled by one thread-block cluster of Ck CTAs that
+//    split its K rows; the grid (strips x Ck) is sized to one wave of the SMs. The
+//    split-K partial sums are reduced on chip through distributed shared memory at
+//    the end, so there is no global workspace, no atomics, and the result is
+//    deterministic.
+//  * One producer thread per CTA streams the strip's super-block rows with 3-D TMA
+//    tile loads (cp.async.bulk.tensor, L2 evict-first) into a ring of shared-memory
+//    stages guarded by mbarriers. The weights never depend on the previous kernel,
+//    so the whole ring is filled before griddepcontrol.wait (programmatic dependent
+//    launch): a CTA of the next call, resident beside this one, prefetches while this
+//    one computes.
+//  * After griddepcontrol.wait the consumer warps stage the CTA's activation slice in
+//    shared memory (one pass, L2 resident) and expand nibbles straight into
+//    mma.m16n8k16 A fragments in registers: byte permute + magic-exponent fp16
+//    conversion + one fp16 multiply by the group scale, bit-exact with the reference
+//    dequant; the batch (padded to 8/16/32) is the MMA n dimension, fp32 accumulate.
+//  * Shared-memory rows are laid out so the fragment loads are bank-conflict free:
+//    full 144-byte super-block rows (WS = 256), or a 16-byte scale row plus a
+//    nibble row padded to 80 / 96 bytes by the TMA box (WS = 128, M % 256 == 128).
 #include <algorithm>
 
 #include "common.cuh"
 
 namespace mb {
 
-constexpr int kSB = 144;                 // bytes per super-block
-constexpr int kStripCols = 256;          // columns per strip (one super-block per row)
-constexpr int kSliceRows = 16;           // k rows per MMA slice
-constexpr int kSliceBytes = kSliceRows * kSB;  // 2304, a multiple of 128
-constexpr int kSlicesPerStage = 4;
-constexpr int kStageWBytes = kSlicesPerStage * kSliceBytes;  // 9216
-constexpr int kConsumerWarps = 4;
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;  // + one producer warp
-constexpr int kRedStride = 256 + 4;        // padded fp32 row of the reduction tile
+constexpr int kSB = 144;        // bytes per super-block
+constexpr int kSliceRows = 16;  // k rows per MMA slice
+constexpr int kSPS = 8;         // slices per full stage (128 rows)
+constexpr int kStageRows = kSPS * kSliceRows;
+constexpr int kMaxStages = 8;
+constexpr int kMaxCk = 8;
 
-struct GemmArgs {
-  uint16_t* out;        // [N, M] fp16
-  float* ws;            // [N, M] fp32 partial sums, zero between calls
-  uint32_t* counters;   // [nstrips]
-  uint32_t* err;        // device error word
-  int N, K, M;
-  int KS;               // k slices per strip
-  long long U;          // total units = nstrips * KS
-  int G;                // grid size
-};
-
-template <int NT>
-struct Cfg {
-  static constexpr int kStages = (NT == 4) ? 4 : 6;
-  static constexpr int kXBytes = 8 * NT * 128;  // [8*NT rows][64 fp16], 128B-swizzled
-  static constexpr int kRedBytes = 8 * NT * kRedStride * 4;
-  static constexpr int kSmem = 1024 + kStages * kXBytes + kStages * kStageWBytes + kRedBytes + 2 * kStages * 8 + 16;
-};
-
-struct StageIter {
-  long long u, end;
-  int KS;
-  __device__ __forceinline__ bool next(int& strip, int& sl, int& n) {
-    if (u >= end) return false;
-    strip = static_cast<int>(u / KS);
-    sl = static_cast<int>(u - static_cast<long long>(strip) * KS);
-    long long m = KS - sl;
-    if (end - u < m) m = end - u;
-    if (m > kSlicesPerStage) m = kSlicesPerStage;
-    n = static_cast<int>(m);
-    u += n;
-    return true;
+// Shared-memory layout of one pipeline stage (128 rows of the CTA's strip).
+//  WS = 256: full 144-byte super-block rows (scales then nibbles), row stride 144 B.
+//  WS = 128 / 64: a 16-byte scale row per k row, then the strip's nibble bytes in a
+//  row padded by the TMA box (80 / 48 bytes for one row phase, 96 / 32 bytes for two)
+//  so that the fragment loads below hit 32 distinct banks. With P = 2 row phases
+//  (M % 256 == 128) rows of each phase are stored together.
+template <int WS, int P>
+struct Layout {
+  static_assert(WS == 256 || WS == 128 || WS == 64, "strip width");
+  static_assert(WS != 256 || P == 1, "a 256-wide strip needs M % 256 == 0");
+  static_assert(P == 1 || P == 2, "row phases");
+  static constexpr int kNibRow = (WS == 128) ? (P == 1 ? 80 : 96) : (P == 1 ? 48 : 32);
+  static constexpr int kScRegion = kStageRows * 16;
+  static constexpr int kStageBytes = (WS == 256) ? kStageRows * kSB : kStageRows * (16 + kNibRow);
+  static constexpr int kRowsPerPhase = kStageRows / P;
+  static __device__ __host__ constexpr int bytes(int n) {  // tx bytes of a stage with n slices
+    return (WS == 256) ? n * kSliceRows * kSB : n * kSliceRows * (16 + kNibRow);
+  }
+  // byte offset of row k's scale chunk / first strip nibble byte within a stage
+  static __device__ __forceinline__ constexpr int sc(int k) {
+    return (WS == 256) ? k * kSB : ((k & (P - 1)) * kRowsPerPhase + k / P) * 16;
+  }
+  static __device__ __forceinline__ constexpr int nib(int k) {
+    return (WS == 256) ? k * kSB + 16 : kScRegion + ((k & (P - 1)) * kRowsPerPhase + k / P) * kNibRow;
   }
 };
 
-__device__ __forceinline__ long long range_begin(long long c, long long U, int G) { return (c * U) / G; }
+struct GemmParams {
+  uint16_t* out;        // [N, M] fp16
+  const uint16_t* act;  // [N, K] fp16
+  uint32_t* err;        // optional device error word (may be null)
+  int N, K, M;
+  int KS;               // k slices (ceil(K / 16))
+  int Ck;               // CTAs per cluster = K split
+  int S;                // stages in the ring
+  int xstride;          // bytes per activation row in shared memory
+  int xbytes;           // activation region
+};
 
-__device__ __forceinline__ int cta_of(long long u, long long U, int G) {
-  long long c = (u * G) / U;
-  while (c + 1 < G && range_begin(c + 1, U, G) <= u) ++c;
-  while (c > 0 && range_begin(c, U, G) > u) --c;
-  return static_cast<int>(c);
-}
-
-__device__ __forceinline__ uint32_t lds_u32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
-__device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+struct WMaps {  // weight tensor maps: full-stage and 16-row boxes (scale / nibble rows)
+  CUtensorMap full_a, full_b, slice_a, slice_b;
+};
 
 template <int NW>
 __device__ __forceinline__ void lds_words(const uint8_t* p, uint32_t (&w)[NW]) {
@@ -100,35 +95,43 @@ __device__ __forceinline__ void lds_words(const uint8_t* p, uint32_t (&w)[NW]) {
     w[0] = *reinterpret_cast<const uint32_t*>(p);
   }
 }
+__device__ __forceinline__ uint32_t lds_u32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
-// One 16-row k slice for this thread's column run.
-//   wsl: slice base (16 rows x 144 B); xt: stage activation tile; j: slice index in stage
-//   colbyte: byte offset of the thread's first nibble in a row; grp: its scale group.
+// One 16-row k slice for this thread's MR-column run.
 // Thread (g4 = lane/4, t4 = lane%4) owns rows 2t4, 2t4+1, 2t4+8, 2t4+9 of the slice
 // (the k positions of the m16n8k16 A fragment) and MR consecutive columns; m16 tile
 // i of the warp maps fragment row g4 to column 2i and row g4+8 to column 2i+1 of the
-// thread's run, so each nibble byte feeds one tile.
-template <int NT>
-__device__ __forceinline__ void consume_slice(const uint8_t* wsl, const uint8_t* xt, int j, int g4, int t4, int colbyte,
-                                              int grp, float (&acc)[16 / NT][NT][4]) {
-  constexpr int NW = 4 / NT;  // 32-bit nibble words per row per thread
-  const uint8_t* r0 = wsl + (2 * t4) * kSB;
-  const uint8_t* r1 = r0 + kSB;
-  const uint8_t* r2 = r0 + 8 * kSB;
-  const uint8_t* r3 = r2 + kSB;
+// run, so each nibble byte feeds exactly one tile and the warp has MR/2 independent
+// accumulator chains per batch tile. The weight operand is fp16((n - 8) * s): exact
+// magic-exponent conversion of the nibble, then one rounding multiply by the group
+// scale — bit-identical to the reference dequant.
+//   stage, k0: stage base and the stage-local row 2t4 of this slice; nb: byte offset
+//   of the run within a nibble row; ge / go: scale index for even / odd rows;
+//   xrow: this lane's activation row (n = 8 nt + g4) at the slice's first k.
+template <int NT, int WS, int P, int MR>
+__device__ __forceinline__ void consume_slice(const uint8_t* stage, int k0, int nb, int ge, int go,
+                                              const uint8_t* const (&xrow)[NT], const bool (&xok)[NT], int t4,
+                                              float (&acc)[MR / 2][NT][4]) {
+  using L = Layout<WS, P>;
+  constexpr int NW = MR / 8;  // 32-bit nibble words per row
+  // rows 2t4, 2t4+1, 2t4+8, 2t4+9 as constant offsets from row 2t4
+  constexpr int dn1 = L::nib(1) - L::nib(0), dn8 = L::nib(8) - L::nib(0), dn9 = L::nib(9) - L::nib(0);
+  constexpr int ds1 = L::sc(1) - L::sc(0), ds8 = L::sc(8) - L::sc(0), ds9 = L::sc(9) - L::sc(0);
+  const uint8_t* pn = stage + L::nib(k0) + nb;
+  const uint8_t* ps = stage + L::sc(k0);
   uint32_t w0[NW], w1[NW], w2[NW], w3[NW];
-  lds_words<NW>(r0 + colbyte, w0);
-  lds_words<NW>(r1 + colbyte, w1);
-  lds_words<NW>(r2 + colbyte, w2);
-  lds_words<NW>(r3 + colbyte, w3);
-  const uint32_t s01 = lds_u16(r0 + 2 * grp) | (lds_u16(r1 + 2 * grp) << 16);
-  const uint32_t s23 = lds_u16(r2 + 2 * grp) | (lds_u16(r3 + 2 * grp) << 16);
+  lds_words<NW>(pn, w0);
+  lds_words<NW>(pn + dn1, w1);
+  lds_words<NW>(pn + dn8, w2);
+  lds_words<NW>(pn + dn9, w3);
+  const uint32_t s01 = lds_u16(ps + 2 * ge) | (lds_u16(ps + ds1 + 2 * go) << 16);
+  const uint32_t s23 = lds_u16(ps + ds8 + 2 * ge) | (lds_u16(ps + ds9 + 2 * go) << 16);
   uint32_t bf[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const uint8_t* xr = xt + (nt * 8 + g4) * 128 + 4 * t4;
-    bf[nt][0] = lds_u32(xr + (((2 * j) ^ g4) << 4));
-    bf[nt][1] = lds_u32(xr + (((2 * j + 1) ^ g4) << 4));
+    bf[nt][0] = xok[nt] ? lds_u32(xrow[nt] + 4 * t4) : 0u;
+    bf[nt][1] = xok[nt] ? lds_u32(xrow[nt] + 16 + 4 * t4) : 0u;
   }
 #pragma unroll
   for (int v = 0; v < NW; ++v) {
@@ -151,197 +154,269 @@ __device__ __forceinline__ void consume_slice(const uint8_t* wsl, const uint8_t*
   }
 }
 
-template <int NT>
-__device__ __forceinline__ void store_half4(uint16_t* dst, float4 v) {
-  const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
-  uint2 u;
-  u.x = *reinterpret_cast<const uint32_t*>(&a);
-  u.y = *reinterpret_cast<const uint32_t*>(&b);
-  *reinterpret_cast<uint2*>(dst) = u;
-}
-
-// Strip epilogue: reduce the four warps' partial sums in shared memory, then either
-// write fp16 directly (this CTA covered the whole strip) or add into the fp32
-// workspace; the last arriving CTA converts the strip to fp16 and re-zeroes it.
-template <int NT>
-__device__ __forceinline__ void strip_epilogue(const GemmArgs& p, int strip, float (&acc)[16 / NT][NT][4],
-                                               float* red, int* flag, int ctid, int g4, int t4, int mbt) {
-  constexpr int MT = 16 / NT;
+template <int WS, int P>
+__device__ __forceinline__ void issue_stage(const WMaps& maps, uint8_t* dst, uint64_t* bar, int k0, int n,
+                                            const int (&ey)[P], const int (&ex)[P], uint64_t pol) {
+  using L = Layout<WS, P>;
+  mbar_expect_tx(bar, L::bytes(n));
+  if constexpr (WS == 256) {
+    if (n == kSPS) {
+      tma_load_3d(dst, &maps.full_a, bar, 0, ey[0], k0, pol);
+    } else {
+      for (int j = 0; j < n; ++j)
+        tma_load_3d(dst + j * kSliceRows * kSB, &maps.slice_a, bar, 0, ey[0], k0 + j * kSliceRows, pol);
+    }
+  } else {
+    constexpr int rp = L::kRowsPerPhase;
 #pragma unroll
-  for (int i = 0; i < MT; ++i)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int n = nt * 8 + 2 * t4 + (c & 1);
-        const int col = mbt + 2 * i + (c >> 1);
-        if (n < p.N) atomicAdd(&red[n * kRedStride + col], acc[i][nt][c]);
-        acc[i][nt][c] = 0.0f;
+    for (int r = 0; r < P; ++r) {
+      uint8_t* sdst = dst + r * rp * 16;
+      uint8_t* ndst = dst + L::kScRegion + r * rp * L::kNibRow;
+      if (n == kSPS) {
+        tma_load_3d(sdst, &maps.full_a, bar, 0, ey[r], k0 / P, pol);
+        tma_load_3d(ndst, &maps.full_b, bar, ex[r], ey[r], k0 / P, pol);
+      } else {
+        constexpr int sp = kSliceRows / P;
+        for (int j = 0; j < n; ++j) {
+          tma_load_3d(sdst + j * sp * 16, &maps.slice_a, bar, 0, ey[r], (k0 + j * kSliceRows) / P, pol);
+          tma_load_3d(ndst + j * sp * L::kNibRow, &maps.slice_b, bar, ex[r], ey[r], (k0 + j * kSliceRows) / P, pol);
+        }
       }
-  named_bar_sync(1, kConsumers);
-
-  const long long s0 = static_cast<long long>(strip) * p.KS;
-  const int first = cta_of(s0, p.U, p.G);
-  const int last = cta_of(s0 + p.KS - 1, p.U, p.G);
-  const int nvec = p.N * (kStripCols / 4);
-  const size_t colbase = static_cast<size_t>(strip) * kStripCols;
-
-  if (first == last) {  // sole owner of the strip
-    for (int idx = ctid; idx < nvec; idx += kConsumers) {
-      const int n = idx >> 6, c4 = (idx & 63) * 4;
-      float4* rp = reinterpret_cast<float4*>(red + n * kRedStride + c4);
-      const float4 v = *rp;
-      *rp = make_float4(0.f, 0.f, 0.f, 0.f);
-      store_half4<NT>(p.out + static_cast<size_t>(n) * p.M + colbase + c4, v);
     }
-    named_bar_sync(1, kConsumers);
-    return;
   }
-
-  for (int idx = ctid; idx < nvec; idx += kConsumers) {
-    const int n = idx >> 6, c4 = (idx & 63) * 4;
-    float4* rp = reinterpret_cast<float4*>(red + n * kRedStride + c4);
-    const float4 v = *rp;
-    *rp = make_float4(0.f, 0.f, 0.f, 0.f);
-    red_add_v4(p.ws + static_cast<size_t>(n) * p.M + colbase + c4, v.x, v.y, v.z, v.w);
-  }
-  __threadfence();
-  named_bar_sync(1, kConsumers);
-  if (ctid == 0) {
-    const uint32_t old = atomicAdd(&p.counters[strip], 1u);
-    *flag = (old == static_cast<uint32_t>(last - first)) ? 1 : 0;
-  }
-  named_bar_sync(1, kConsumers);
-  if (*flag) {
-    __threadfence();
-    for (int idx = ctid; idx < nvec; idx += kConsumers) {
-      const int n = idx >> 6, c4 = (idx & 63) * 4;
-      float4* gp = reinterpret_cast<float4*>(p.ws + static_cast<size_t>(n) * p.M + colbase + c4);
-      const float4 v = __ldcg(gp);
-      __stcg(gp, make_float4(0.f, 0.f, 0.f, 0.f));
-      store_half4<NT>(p.out + static_cast<size_t>(n) * p.M + colbase + c4, v);
-    }
-    if (ctid == 0) atomicExch(&p.counters[strip], 0u);
-  }
-  named_bar_sync(1, kConsumers);
 }
 
-template <int NT>
-__global__ void __launch_bounds__(kThreads, 1)
-    k_gemm_tma(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, const GemmArgs p) {
-  using C = Cfg<NT>;
-  constexpr int S = C::kStages;
+__device__ __forceinline__ void store_half2(uint16_t* dst, float a, float b) {
+  const __half2 x = __floats2half2_rn(a, b);
+  *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(&x);
+}
+
+// Columns per thread run for (NT, WS): 32 / NT, at most WS / 8 (eight runs per warp).
+template <int NT, int WS>
+struct RunCols {
+  static constexpr int v = (32 / NT < WS / 8) ? 32 / NT : WS / 8;
+};
+
+// NT: n-tiles of 8 batch rows (1, 2, 4); WS: strip width; P: row phases (1, 2);
+// CW: consumer warps. __launch_bounds__(.., 2): a CTA uses at most half an SM's
+// registers so the next call's CTAs (launched early through PDL) can be resident
+// and prefetch their weights while this one computes.
+template <int NT, int WS, int P, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32, 2)
+    k_gemm_int4(const __grid_constant__ WMaps maps, const GemmParams p) {
+  using L = Layout<WS, P>;
+  constexpr int MR = RunCols<NT, WS>::v;  // columns per thread run
+  constexpr int kTiles = MR / 2;          // m16 tiles per warp
+  constexpr int kCm = WS / (8 * MR);      // column parts per strip (one warp each)
+  constexpr int kKG = CW / kCm;           // warps sharing a column part (k groups)
+  static_assert(kCm * kKG == CW, "warp layout");
+  constexpr int kRegs = kTiles * NT * 4;  // accumulators per thread
+  constexpr int kThreads = (CW + 1) * 32;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* xs = smem;
-  uint8_t* wsm = xs + S * C::kXBytes;
-  float* red = reinterpret_cast<float*>(wsm + S * kStageWBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + C::kRedBytes);
-  uint64_t* empty = full + S;
-  int* flag = reinterpret_cast<int*>(empty + S);
+  uint8_t* stages = smem;
+  uint8_t* xs = stages + p.S * L::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(xs + p.xbytes);
+  uint64_t* empty = full + kMaxStages;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long b0 = range_begin(blockIdx.x, p.U, p.G);
-  const long long b1 = range_begin(blockIdx.x + 1, p.U, p.G);
+  const int strip = blockIdx.x / p.Ck;
+  const int q = blockIdx.x - strip * p.Ck;  // == rank in the cluster (cluster dims = (Ck,1,1))
+  const int sl0 = static_cast<int>((static_cast<long long>(q) * p.KS) / p.Ck);
+  const int sl1 = static_cast<int>((static_cast<long long>(q + 1) * p.KS) / p.Ck);
+  const int nst = (sl1 - sl0 + kSPS - 1) / kSPS;
+  const int c0 = strip * WS;
+  // per row phase: super-block index within a period (y), first nibble byte of the
+  // strip in that super-block (x) and the scale index of the strip's first column
+  int ey[P], ex[P], grp[P];
+#pragma unroll
+  for (int r = 0; r < P; ++r) {
+    const long long f = static_cast<long long>(r) * p.M + c0;
+    ey[r] = static_cast<int>(f >> 8);
+    const int e = static_cast<int>(f & 255);
+    ex[r] = 16 + e / 2;
+    grp[r] = e / 32;
+  }
 
   if (threadIdx.x == 0) {
-#pragma unroll
-    for (int s = 0; s < S; ++s) {
+    for (int s = 0; s < p.S; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(empty + s, kConsumerWarps);
+      mbar_init(empty + s, CW);
     }
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < 8 * NT * kRedStride; i += kThreads) red[i] = 0.0f;
   __syncthreads();
   pdl_launch_dependents();
 
-  if (warp == kConsumerWarps) {
-    // ---------------- producer ----------------
-    if (lane != 0) return;
-    const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
-    StageIter it{b0, b1, p.KS};
-    int strip, sl, n;
-    int pre_sl[S];
-    int npre = 0;
-    while (npre < S && it.next(strip, sl, n)) {
-      mbar_expect_tx(full + npre, n * kSliceBytes + C::kXBytes);
-      for (int j = 0; j < n; ++j)
-        tma_load_2d(wsm + npre * kStageWBytes + j * kSliceBytes, &wmap, full + npre, strip * kSB,
-                    (sl + j) * kSliceRows, pol_w);
-      pre_sl[npre++] = sl;
+  float* slots = reinterpret_cast<float*>(stages);  // final reduction scratch (ring + activations)
+  if (warp == CW) {
+    // ---------------- producer: weights only, no dependency on the previous grid ----
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      for (int st = 0; st < nst; ++st) {
+        const int s = st % p.S;
+        if (st >= p.S && !mbar_wait(empty + s, ((st / p.S) - 1) & 1) && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
+        const int sl = sl0 + st * kSPS;
+        issue_stage<WS, P>(maps, stages + s * L::kStageBytes, full + s, sl * kSliceRows, min(kSPS, sl1 - sl), ey, ex,
+                           pol);
+      }
     }
-    pdl_wait();  // activations may be written by the previous grid
-    for (int s = 0; s < npre; ++s) tma_load_2d(xs + s * C::kXBytes, &xmap, full + s, pre_sl[s] * kSliceRows, 0, pol_x);
-    int i = npre;
-    while (it.next(strip, sl, n)) {
-      const int s = i % S;
-      if (!mbar_wait(empty + s, ((i / S) - 1) & 1)) atomicOr(p.err, MB_DEVERR_TIMEOUT);
-      mbar_expect_tx(full + s, n * kSliceBytes + C::kXBytes);
-      for (int j = 0; j < n; ++j)
-        tma_load_2d(wsm + s * kStageWBytes + j * kSliceBytes, &wmap, full + s, strip * kSB, (sl + j) * kSliceRows,
-                    pol_w);
-      tma_load_2d(xs + s * C::kXBytes, &xmap, full + s, sl * kSliceRows, 0, pol_x);
-      ++i;
+    __syncwarp();
+  } else {
+    // ---------------- consumers ----------------
+    const int g4 = lane >> 2, t4 = lane & 3;
+    const int mpart = warp % kCm, kg = warp / kCm;
+    const int mcol = mpart * 8 * MR + g4 * MR;  // first column of this thread's run in the strip
+    const int nb = (WS == 256) ? mcol / 2 : mcol / 2;
+    const int ge = grp[0] + mcol / 32, go = grp[P - 1] + mcol / 32;
+
+    pdl_wait();  // activations may come from the previous grid; all writes follow it
+    // stage this CTA's activation slice [N][k0, k1) in shared memory (zero past K)
+    const int k0 = sl0 * kSliceRows;
+    const int chunks = (sl1 - sl0) * kSliceRows / 8;  // 16-byte chunks per row
+    for (int idx = threadIdx.x; idx < p.N * chunks; idx += CW * 32) {
+      const int n = idx / chunks, c = idx - n * chunks;
+      const int k = k0 + c * 8;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (k < p.K) v = __ldg(reinterpret_cast<const uint4*>(p.act + static_cast<size_t>(n) * p.K + k));
+      *reinterpret_cast<uint4*>(xs + n * p.xstride + c * 16) = v;
+    }
+    named_bar_sync(1, CW * 32);
+
+    float acc[kTiles][NT][4];
+#pragma unroll
+    for (int i = 0; i < kTiles; ++i)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[i][nt][c] = 0.0f;
+    bool xok[NT];
+    const uint8_t* xbase[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int n = nt * 8 + g4;
+      xok[nt] = n < p.N;
+      xbase[nt] = xs + (xok[nt] ? n : 0) * p.xstride;
+    }
+
+    for (int st = 0; st < nst; ++st) {
+      const int s = st % p.S;
+      if (!mbar_wait(full + s, (st / p.S) & 1) && lane == 0 && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
+      const uint8_t* stage = stages + s * L::kStageBytes;
+      const int n = min(kSPS, sl1 - (sl0 + st * kSPS));
+      for (int j = kg; j < n; j += kKG) {
+        const int kx = (st * kSPS + j) * kSliceRows;  // k offset within the activation slice
+        const uint8_t* xr[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) xr[nt] = xbase[nt] + kx * 2;
+        consume_slice<NT, WS, P, MR>(stage, j * kSliceRows + 2 * t4, nb, ge, go, xr, xok, t4, acc);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + s);
+    }
+
+    // park the partial sums (lane-major: conflict free) once every warp is done with
+    // the stage ring and the activation slice
+    named_bar_sync(1, CW * 32);
+    float* slot = slots + warp * kRegs * 32 + lane;
+#pragma unroll
+    for (int i = 0; i < kTiles; ++i)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) slot[((i * NT + nt) * 4 + c) * 32] = acc[i][nt][c];
+  }
+  __syncthreads();
+
+  // ---- reduction: k groups of this CTA, then the Ck CTAs of the cluster ----
+  // Work item = (part, tile i, nt, row parity r, lane): columns 2i and 2i+1 of one
+  // output row (c = r and c = r + 2), written as one half2.
+  constexpr int kItems = kCm * kTiles * NT * 2 * 32;
+  const int sum_off = CW * kRegs * 32;  // per-CTA sums after the k-group slots
+  if (p.Ck == 1) {
+    for (int e = threadIdx.x; e < kItems; e += kThreads) {
+      const int ln = e & 31;
+      int t = e >> 5;
+      const int r = t & 1;
+      t >>= 1;
+      const int nt = t % NT;
+      t /= NT;
+      const int i = t % kTiles;
+      const int mp = t / kTiles;
+      const int n = nt * 8 + 2 * (ln & 3) + r;
+      if (n >= p.N) continue;
+      const int reg = (i * NT + nt) * 4 + r;
+      float lo = 0.0f, hi = 0.0f;
+#pragma unroll 4
+      for (int g = 0; g < kKG; ++g) {
+        const float* sl = slots + (g * kCm + mp) * kRegs * 32 + ln;
+        lo += sl[reg * 32];
+        hi += sl[(reg + 2) * 32];
+      }
+      const int col = c0 + mp * 8 * MR + (ln >> 2) * MR + 2 * i;
+      store_half2(p.out + static_cast<size_t>(n) * p.M + col, lo, hi);
     }
     return;
   }
-
-  // ---------------- consumers ----------------
-  constexpr int MR = 32 / NT;  // columns per thread per row
-  constexpr int MT = MR / 2;   // m16 tiles per warp
-  const int g4 = lane >> 2, t4 = lane & 3;
-  const int mpart = warp % NT;
-  const int slice0 = warp / NT;
-  constexpr int slice_step = kConsumerWarps / NT;
-  const int mbt = mpart * (kStripCols / NT) + g4 * MR;
-  const int colbyte = 16 + mbt / 2;
-  const int grp = mbt / 32;
-  float acc[MT][NT][4];
-#pragma unroll
-  for (int i = 0; i < MT; ++i)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[i][nt][c] = 0.0f;
-
-  pdl_wait();  // all global writes below happen after the previous grid completed
-  StageIter it{b0, b1, p.KS};
-  int strip, sl, n, i = 0;
-  while (it.next(strip, sl, n)) {
-    const int s = i % S;
-    if (!mbar_wait(full + s, (i / S) & 1) && lane == 0) atomicOr(p.err, MB_DEVERR_TIMEOUT);
-    const uint8_t* wst = wsm + s * kStageWBytes;
-    const uint8_t* xt = xs + s * C::kXBytes;
-    for (int j = slice0; j < n; j += slice_step) consume_slice<NT>(wst + j * kSliceBytes, xt, j, g4, t4, colbyte, grp, acc);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty + s);
-    ++i;
-    if (it.u == it.end || (it.u % p.KS) == 0) strip_epilogue<NT>(p, strip, acc, red, flag, threadIdx.x, g4, t4, mbt);
+  // in-CTA: sum the k groups into this CTA's partial tile
+  for (int e = threadIdx.x; e < kCm * kRegs * 32; e += kThreads) {
+    const int ln = e & 31, reg = (e >> 5) % kRegs, mp = (e >> 5) / kRegs;
+    float v = 0.0f;
+#pragma unroll 4
+    for (int g = 0; g < kKG; ++g) v += slots[((g * kCm + mp) * kRegs + reg) * 32 + ln];
+    slots[sum_off + e] = v;
   }
+  cluster_sync();
+  {
+    const int per = (kItems + p.Ck - 1) / p.Ck;
+    const int e0 = q * per, e1 = min(kItems, e0 + per);
+    const uint32_t base = smem_u32(slots + sum_off);
+    for (int e = e0 + static_cast<int>(threadIdx.x); e < e1; e += kThreads) {
+      const int ln = e & 31;
+      int t = e >> 5;
+      const int r = t & 1;
+      t >>= 1;
+      const int nt = t % NT;
+      t /= NT;
+      const int i = t % kTiles;
+      const int mp = t / kTiles;
+      const int n = nt * 8 + 2 * (ln & 3) + r;
+      if (n >= p.N) continue;
+      const int il = (mp * kRegs + (i * NT + nt) * 4 + r) * 32 + ln;
+      float lo = 0.0f, hi = 0.0f;
+      for (int c = 0; c < p.Ck; ++c) {
+        const uint32_t a = mapa_shared(base, static_cast<uint32_t>(c));
+        lo += ld_shared_cluster_f32(a + 4u * il);
+        hi += ld_shared_cluster_f32(a + 4u * (il + 64));
+      }
+      const int col = c0 + mp * 8 * MR + (ln >> 2) * MR + 2 * i;
+      store_half2(p.out + static_cast<size_t>(n) * p.M + col, lo, hi);
+    }
+  }
+  cluster_sync();  // peers may still be reading this CTA's sums
 }
 
 // ---------------------------------------------------------------------------
-// Generic path (any M with K*M % 256 == 0; K not a multiple of 8): one thread per
-// output column, flat super-block indexing as in fused_batched_gemm_int4
-// (batched_gemm.metal:146-155), activations staged in shared memory. Correct for
-// every shape; the TMA path above is the fast one.
+// Generic path (any M with K*M % 256 == 0, any K): one thread per output column,
+// flat super-block indexing as in fused_batched_gemm_int4 (batched_gemm.metal:146-155),
+// activations staged in shared memory. Correct for every shape; the TMA path above
+// is the fast one.
 // ---------------------------------------------------------------------------
 template <int NB>
 __global__ void __launch_bounds__(128) k_gemm_generic(const uint16_t* __restrict__ act, const uint8_t* __restrict__ sb,
                                                       uint16_t* __restrict__ out, int N, int K, int M) {
   constexpr int KC = 64;
-  __shared__ float xs[NB][KC];
+  __shared__ float xsm[NB][KC];
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   float acc[NB];
 #pragma unroll
   for (int n = 0; n < NB; ++n) acc[n] = 0.0f;
-  pdl_wait();
   for (int k0 = 0; k0 < K; k0 += KC) {
     __syncthreads();
     for (int t = threadIdx.x; t < NB * KC; t += blockDim.x) {
       const int n = t / KC, kk = t % KC;
-      xs[n][kk] = (n < N && k0 + kk < K) ? __half2float(__ushort_as_half(act[static_cast<size_t>(n) * K + k0 + kk])) : 0.0f;
+      xsm[n][kk] = (n < N && k0 + kk < K) ? __half2float(__ushort_as_half(act[static_cast<size_t>(n) * K + k0 + kk]))
+                                          : 0.0f;
     }
     __syncthreads();
     if (m < M) {
@@ -351,11 +426,11 @@ __global__ void __launch_bounds__(128) k_gemm_generic(const uint16_t* __restrict
         const uint8_t* b = sb + (flat >> 8) * kSB;
         const int e = static_cast<int>(flat & 255);
         const int byte = __ldg(b + 16 + (e >> 1));
-        const int q = ((e & 1) ? (byte >> 4) : (byte & 15)) - 8;
+        const int qv = ((e & 1) ? (byte >> 4) : (byte & 15)) - 8;
         const __half s = __ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(b) + (e >> 5)));
-        const float w = __half2float(__hmul(__int2half_rn(q), s));
+        const float w = __half2float(__hmul(__int2half_rn(qv), s));
 #pragma unroll
-        for (int n = 0; n < NB; ++n) acc[n] = fmaf(xs[n][kk], w, acc[n]);
+        for (int n = 0; n < NB; ++n) acc[n] = fmaf(xsm[n][kk], w, acc[n]);
       }
     }
   }
@@ -368,81 +443,155 @@ __global__ void __launch_bounds__(128) k_gemm_generic(const uint16_t* __restrict
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-static constexpr size_t kWsHeader = 256;
+struct Plan {
+  int ws = 0, P = 1, Ck = 1, nt = 1, S = 0, smem = 0, xstride = 0, xbytes = 0, ctas = 0;
+  bool fast = false;
+};
 
-static inline size_t ws_counters_bytes(int M) {
-  const size_t nstrips = (static_cast<size_t>(M) + kStripCols - 1) / kStripCols;
-  return (nstrips * 4 + 255) / 256 * 256;
+static constexpr int kCW = 8;                   // consumer warps per CTA
+static constexpr int kSmemBudget = 112 * 1024;  // half an SM: room for the next call's CTA
+
+static int stage_bytes_of(int ws, int P) {
+  if (ws == 256) return Layout<256, 1>::kStageBytes;
+  return P == 1 ? Layout<128, 1>::kStageBytes : Layout<128, 2>::kStageBytes;
 }
 
-static inline bool tma_path_ok(const void* act, const void* sb, int K, int M) {
-  return M % kStripCols == 0 && K % 8 == 0 && aligned(act, 16) && aligned(sb, 16);
+// bytes of the final-reduction scratch (k-group slots + per-CTA sums), which reuses
+// the stage ring and the activation slice
+static int reduce_bytes(int nt, int ws) {
+  const int mr = std::min(32 / nt, ws / 8);
+  const int regs = (mr / 2) * nt * 4;
+  const int cm = ws / (8 * mr);
+  return (kCW + cm) * regs * 32 * 4;
 }
 
-// Resident CTAs per SM for k_gemm_tma<NT> on the current device (capped at 2 so a
-// dependent grid launched with PDL finds room to start its prefetch). The first call
-// on a device also raises the kernel's dynamic shared-memory limit there.
-template <int NT>
-static int blocks_per_sm() {
-  static int per_dev[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
-  if (per_dev[dev] == 0) {
-    if (cudaFuncSetAttribute(k_gemm_tma<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<NT>::kSmem) !=
-        cudaSuccess)
-      return 0;
-    int b = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, k_gemm_tma<NT>, kThreads, Cfg<NT>::kSmem) != cudaSuccess)
-      return 0;
-    per_dev[dev] = std::max(1, std::min(b, 2));
+// Picks the strip width, K split (cluster size) and ring depth for a shape: the most
+// CTAs that fit one wave of the SMs (all SMs stream the weights), then no cluster
+// (no cross-CTA reduction), then the wider strip (activations read fewer times).
+static Plan plan_gemm(int N, int K, int M, int sms) {
+  Plan pl;
+  pl.nt = N <= 8 ? 1 : (N <= 16 ? 2 : 4);
+  if (K % 8 != 0 || M % 128 != 0) return pl;
+  const int P = (M % 256 == 0) ? 1 : ((M % 128 == 0) ? 2 : 0);
+  if (P == 0) return pl;
+  const int KS = (K + kSliceRows - 1) / kSliceRows;
+  long long best_key = -1;
+  for (int ws : {256, 128}) {
+    if (ws == 256 && P != 1) continue;
+    const int strips = M / ws;
+    for (int ck = 1; ck <= kMaxCk && ck <= KS; ++ck) {
+      const long long ctas = static_cast<long long>(strips) * ck;
+      if (ck > 1 && ctas > sms) break;
+      const int slices = (KS + ck - 1) / ck;
+      const int xstride = slices * kSliceRows * 2 + 16;
+      const int xbytes = (N * xstride + 127) / 128 * 128;
+      if (xbytes + 2 * stage_bytes_of(ws, P) + 2048 > kSmemBudget) continue;
+      const long long used = std::min<long long>(ctas, sms);
+      // one wave: more SMs first (quantised to 1/16 of the SMs), then wider strips
+      // (wider per-thread runs: fewer instructions per weight), then fewer CTAs per
+      // cluster
+      const long long key = (used * 16 / sms) * 1000 + ws / 64 * 10 + (8 - ck);
+      if (key > best_key) {
+        best_key = key;
+        pl.ws = ws;
+        pl.Ck = ck;
+        pl.xstride = xstride;
+        pl.xbytes = xbytes;
+        pl.ctas = static_cast<int>(ctas);
+      }
+    }
   }
-  return per_dev[dev];
+  if (best_key < 0) return pl;
+  pl.P = P;
+  const int sb = stage_bytes_of(pl.ws, P);
+  const int KSc = (KS + pl.Ck - 1) / pl.Ck;
+  const int need = (KSc + kSPS - 1) / kSPS;  // stages that hold the CTA's whole slice
+  int S = (kSmemBudget - 2048 - pl.xbytes) / sb;
+  S = std::max(2, std::min(std::min(S, kMaxStages), need));
+  // the reduction scratch lives in the stage ring followed by the activation slice
+  while (S * sb + pl.xbytes < reduce_bytes(pl.nt, pl.ws) && S < kMaxStages) ++S;
+  if (S * sb + pl.xbytes < reduce_bytes(pl.nt, pl.ws)) pl.xbytes = reduce_bytes(pl.nt, pl.ws) - S * sb;
+  pl.S = S;
+  pl.smem = 1024 + S * sb + pl.xbytes + 2 * kMaxStages * 8;
+  pl.fast = true;
+  return pl;
 }
 
-template <int NT>
-static int grid_size(long long U) {
-  const int b = blocks_per_sm<NT>();
-  if (b == 0) return 0;
-  const long long g = static_cast<long long>(b) * sm_count();
-  return static_cast<int>(std::min<long long>(g, U));
-}
-
-template <int NT>
-static int launch_tma(const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M, uint8_t* ws,
-                      cudaStream_t st) {
-  CUtensorMap wmap, xmap;
-  const uint64_t row_bytes = static_cast<uint64_t>(M / kStripCols) * kSB;
-  if (!encode_tmap_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, sb, row_bytes, K, row_bytes, kSB, kSliceRows,
-                      CU_TENSOR_MAP_SWIZZLE_NONE))
-    return MB_ERR_LAUNCH;
-  if (!encode_tmap_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, K, N, static_cast<uint64_t>(K) * 2, 64, 8 * NT,
-                      CU_TENSOR_MAP_SWIZZLE_128B))
-    return MB_ERR_LAUNCH;
-  GemmArgs a;
-  a.out = out;
-  a.err = reinterpret_cast<uint32_t*>(ws);
-  a.counters = reinterpret_cast<uint32_t*>(ws + kWsHeader);
-  a.ws = reinterpret_cast<float*>(ws + kWsHeader + ws_counters_bytes(M));
-  a.N = N;
-  a.K = K;
-  a.M = M;
-  a.KS = (K + kSliceRows - 1) / kSliceRows;
-  a.U = static_cast<long long>(M / kStripCols) * a.KS;
-  a.G = grid_size<NT>(a.U);
-  if (a.G <= 0) return MB_ERR_LAUNCH;
+template <int NT, int WS, int P>
+static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M,
+                       uint32_t* err, cudaStream_t st) {
+  using L = Layout<WS, P>;
+  auto kern = k_gemm_int4<NT, WS, P, kCW>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MB_ERR_LAUNCH;
+  if (!attr_set[dev]) {
+    // full shared-memory carveout, so two ~112 KB CTAs (this call and the next) fit an SM
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+      return MB_ERR_LAUNCH;
+    attr_set[dev] = true;
+  }
+  WMaps maps;
+  // 3-D view of the stream: [144 bytes][super-blocks per period][periods of P rows]
+  const uint64_t sbp = static_cast<uint64_t>(P) * M / 256;
+  const uint64_t dims[3] = {kSB, sbp, static_cast<uint64_t>(K / P)};
+  const uint64_t strides[2] = {kSB, sbp * kSB};
+  bool ok;
+  if (WS == 256) {
+    const uint32_t bf[3] = {kSB, 1, kStageRows}, bs[3] = {kSB, 1, kSliceRows};
+    ok = encode_tmap_3d_u8(&maps.full_a, sb, dims, strides, bf) &&
+         encode_tmap_3d_u8(&maps.slice_a, sb, dims, strides, bs);
+    maps.full_b = maps.full_a;
+    maps.slice_b = maps.slice_a;
+  } else {
+    const uint32_t sf[3] = {16, 1, kStageRows / P}, ss[3] = {16, 1, kSliceRows / P};
+    const uint32_t nf[3] = {L::kNibRow, 1, kStageRows / P}, ns[3] = {L::kNibRow, 1, kSliceRows / P};
+    ok = encode_tmap_3d_u8(&maps.full_a, sb, dims, strides, sf) &&
+         encode_tmap_3d_u8(&maps.slice_a, sb, dims, strides, ss) &&
+         encode_tmap_3d_u8(&maps.full_b, sb, dims, strides, nf) &&
+         encode_tmap_3d_u8(&maps.slice_b, sb, dims, strides, ns);
+  }
+  if (!ok) return MB_ERR_LAUNCH;
+  GemmParams prm;
+  prm.out = out;
+  prm.act = act;
+  prm.err = err;
+  prm.N = N;
+  prm.K = K;
+  prm.M = M;
+  prm.KS = (K + kSliceRows - 1) / kSliceRows;
+  prm.Ck = pl.Ck;
+  prm.S = pl.S;
+  prm.xstride = pl.xstride;
+  prm.xbytes = pl.xbytes;
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.G);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = Cfg<NT>::kSmem;
+  cfg.gridDim = dim3((M / WS) * pl.Ck);
+  cfg.blockDim = dim3((kCW + 1) * 32);
+  cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = pl.Ck;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, k_gemm_tma<NT>, wmap, xmap, a) != cudaSuccess) return MB_ERR_LAUNCH;
+  cfg.numAttrs = 2;
+  if (cudaLaunchKernelEx(&cfg, kern, maps, prm) != cudaSuccess) return MB_ERR_LAUNCH;
   return launch_status();
+}
+
+template <int NT>
+static int dispatch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M,
+                         uint32_t* err, cudaStream_t st) {
+  if (pl.ws == 256) return launch_fast<NT, 256, 1>(pl, act, sb, out, N, K, M, err, st);
+  if (pl.ws == 128)
+    return pl.P == 1 ? launch_fast<NT, 128, 1>(pl, act, sb, out, N, K, M, err, st)
+                     : launch_fast<NT, 128, 2>(pl, act, sb, out, N, K, M, err, st);
+  return MB_ERR_UNSUPPORTED;
 }
 
 static int launch_generic(const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M, cudaStream_t st) {
@@ -456,57 +605,52 @@ static int launch_generic(const uint16_t* act, const uint8_t* sb, uint16_t* out,
   return launch_status();
 }
 
+// One launch over up to 32 batch rows.
+static int gemm_rows(const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M, uint32_t* err,
+                     cudaStream_t st) {
+  if (aligned(act, 16) && aligned(sb, 16) && aligned(out, 4)) {
+    const Plan pl = plan_gemm(N, K, M, sm_count());
+    if (pl.fast) {
+      if (pl.nt == 1) return dispatch_fast<1>(pl, act, sb, out, N, K, M, err, st);
+      if (pl.nt == 2) return dispatch_fast<2>(pl, act, sb, out, N, K, M, err, st);
+      return dispatch_fast<4>(pl, act, sb, out, N, K, M, err, st);
+    }
+  }
+  return launch_generic(act, sb, out, N, K, M, st);
+}
+
 }  // namespace mb
 
 using namespace mb;
 
 extern "C" {
 
-size_t mb_int4_gemm_workspace_size(int32_t N, int32_t K, int32_t M) {
-  (void)K;
-  if (N < 1 || M < 1) return 0;
-  const size_t rows = static_cast<size_t>(std::min(N, 32));
-  return kWsHeader + ws_counters_bytes(M) + rows * static_cast<size_t>(M) * 4;
-}
-
 int32_t mb_int4_gemm(const uint16_t* act, const uint8_t* sb, uint16_t* out, int32_t N, int32_t K, int32_t M,
-                     void* workspace, size_t workspace_bytes, void* stream) {
-  if (!act || !sb || !out) return MB_ERR_NULL;
+                     uint32_t* dev_err, void* stream) {
   if (N < 1 || K < 1 || M < 1 || (static_cast<int64_t>(K) * M) % 256 != 0) return MB_ERR_ARGS;
+  if (!act || !sb || !out) return MB_ERR_NULL;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool tma = tma_path_ok(act, sb, K, M);
-  if (tma) {
-    if (!workspace) return MB_ERR_NULL;
-    if (!aligned(workspace, 256) || !aligned(out, 8)) return MB_ERR_ALIGN;
-    if (workspace_bytes < mb_int4_gemm_workspace_size(N, K, M)) return MB_ERR_WORKSPACE;
-  }
   for (int r0 = 0; r0 < N; r0 += 32) {
     const int nb = std::min(32, N - r0);
-    const uint16_t* a = act + static_cast<size_t>(r0) * K;
-    uint16_t* o = out + static_cast<size_t>(r0) * M;
-    int rc;
-    if (tma && aligned(a, 16)) {
-      uint8_t* ws = static_cast<uint8_t*>(workspace);
-      if (nb <= 8)
-        rc = launch_tma<1>(a, sb, o, nb, K, M, ws, st);
-      else if (nb <= 16)
-        rc = launch_tma<2>(a, sb, o, nb, K, M, ws, st);
-      else
-        rc = launch_tma<4>(a, sb, o, nb, K, M, ws, st);
-    } else {
-      rc = launch_generic(a, sb, o, nb, K, M, st);
-    }
+    const int rc = gemm_rows(act + static_cast<size_t>(r0) * K, sb, out + static_cast<size_t>(r0) * M, nb, K, M,
+                             dev_err, st);
     if (rc != MB_OK) return rc;
   }
   return MB_OK;
 }
 
-int32_t mb_int4_gemm_device_status(void* workspace, uint32_t* status_out, void* stream) {
-  if (!workspace || !status_out) return MB_ERR_NULL;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaMemcpyAsync(status_out, workspace, 4, cudaMemcpyDeviceToHost, st) != cudaSuccess) return MB_ERR_LAUNCH;
-  if (cudaMemsetAsync(workspace, 0, 4, st) != cudaSuccess) return MB_ERR_LAUNCH;
-  if (cudaStreamSynchronize(st) != cudaSuccess) return MB_ERR_LAUNCH;
+int32_t mb_int4_gemm_plan(int32_t N, int32_t K, int32_t M, int32_t* info) {
+  if (!info) return MB_ERR_NULL;
+  if (N < 1 || K < 1 || M < 1) return MB_ERR_ARGS;
+  const Plan pl = plan_gemm(std::min(N, 32), K, M, sm_count());
+  info[0] = pl.fast ? 1 : 0;
+  info[1] = pl.ws;
+  info[2] = pl.Ck;
+  info[3] = pl.fast ? pl.ctas : (M + 127) / 128;
+  info[4] = pl.S;
+  info[5] = pl.smem;
+  info[6] = pl.P;
+  info[7] = pl.nt;
   return MB_OK;
 }
 

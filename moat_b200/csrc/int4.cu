@@ -54,6 +54,20 @@ bool encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* bas
   return r == CUDA_SUCCESS;
 }
 
+bool encode_tmap_3d_u8(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
+                       const uint32_t box[3]) {
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t st[2] = {strides[0], strides[1]};
+  cuuint32_t b[3] = {box[0], box[1], box[2]};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), d, st, b, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 static inline int grid_for(int64_t work, int per_block) {
   int64_t b = (work + per_block - 1) / per_block;
   const int64_t cap = static_cast<int64_t>(sm_count()) * 32;
@@ -287,9 +301,9 @@ const char* mb_status_string(int32_t s) {
 
 int32_t mb_int4_quantize(const void* w, int32_t w_is_fp16, int64_t n, int32_t variant, int8_t* q_out,
                          uint16_t* scales_out, uint8_t* sb_out, void* stream) {
-  if (!w || (!q_out && !scales_out && !sb_out)) return MB_ERR_NULL;
   if (n < 0 || n % 32 != 0 || (sb_out && n % 256 != 0) || (variant != 0 && variant != 1)) return MB_ERR_ARGS;
   if (n == 0) return MB_OK;
+  if (!w || (!q_out && !scales_out && !sb_out)) return MB_ERR_NULL;
   const int64_t ngroups = n / 32;
   k_quantize<<<grid_for(ngroups, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(w, w_is_fp16, ngroups, variant,
                                                                                   q_out, scales_out, sb_out);
@@ -297,48 +311,48 @@ int32_t mb_int4_quantize(const void* w, int32_t w_is_fp16, int64_t n, int32_t va
 }
 
 int32_t mb_int4_pack(const int8_t* q, const uint16_t* scales, int64_t n, uint8_t* sb_out, void* stream) {
-  if (!q || !scales || !sb_out) return MB_ERR_NULL;
   if (n < 0 || n % 256 != 0) return MB_ERR_ARGS;
-  if (!aligned(q, 16) || !aligned(scales, 16) || !aligned(sb_out, 16)) return MB_ERR_ALIGN;
   if (n == 0) return MB_OK;
+  if (!q || !scales || !sb_out) return MB_ERR_NULL;
+  if (!aligned(q, 16) || !aligned(scales, 16) || !aligned(sb_out, 16)) return MB_ERR_ALIGN;
   const int64_t nsb = n / 256;
   k_pack<<<grid_for(nsb * 9, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(q, scales, nsb, sb_out);
   return launch_status();
 }
 
 int32_t mb_int4_unpack(const uint8_t* sb, int64_t nsb, int8_t* q_out, uint16_t* scales_out, void* stream) {
-  if (!sb || (!q_out && !scales_out)) return MB_ERR_NULL;
   if (nsb < 0) return MB_ERR_ARGS;
+  if (nsb == 0) return MB_OK;
+  if (!sb || (!q_out && !scales_out)) return MB_ERR_NULL;
   if (!aligned(sb, 16) || (q_out && !aligned(q_out, 16)) || (scales_out && !aligned(scales_out, 16)))
     return MB_ERR_ALIGN;
-  if (nsb == 0) return MB_OK;
   k_unpack<<<grid_for(nsb * 9, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(sb, nsb, q_out, scales_out);
   return launch_status();
 }
 
 int32_t mb_int4_dequant(const uint8_t* sb, uint16_t* out, int64_t nsb, void* stream) {
-  if (!sb || !out) return MB_ERR_NULL;
   if (nsb < 0) return MB_ERR_ARGS;
-  if (!aligned(sb, 16) || !aligned(out, 16)) return MB_ERR_ALIGN;
   if (nsb == 0) return MB_OK;
+  if (!sb || !out) return MB_ERR_NULL;
+  if (!aligned(sb, 16) || !aligned(out, 16)) return MB_ERR_ALIGN;
   k_dequant<<<grid_for(nsb * 8, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(sb, nsb, out);
   return launch_status();
 }
 
 int32_t mb_int4_dequant_q(const int8_t* q, const uint16_t* scales, int64_t n, int32_t group, uint16_t* out,
                           void* stream) {
-  if (!q || !scales || !out) return MB_ERR_NULL;
   if (n < 0 || group < 1 || n % group != 0) return MB_ERR_ARGS;
   if (n == 0) return MB_OK;
+  if (!q || !scales || !out) return MB_ERR_NULL;
   k_dequant_q<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(q, scales, n, group, out);
   return launch_status();
 }
 
 int32_t mb_lut_gather_f16(const int32_t* idx, int64_t n, const uint16_t* lut, int64_t lut_rows, int32_t lut_cols,
                           int64_t group_len, uint16_t* out, void* stream) {
-  if (!idx || !lut || !out) return MB_ERR_NULL;
   if (n < 0 || lut_rows < 1 || lut_cols < 1 || group_len < 1) return MB_ERR_ARGS;
   if (n == 0) return MB_OK;
+  if (!idx || !lut || !out) return MB_ERR_NULL;
   k_lut_gather<<<grid_for(n, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(idx, n, lut, lut_rows, lut_cols,
                                                                                 group_len, out);
   return launch_status();

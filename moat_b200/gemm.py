@@ -20,19 +20,22 @@ import numpy as np
 from . import _lib
 from ._lib import check, lib, ptr, stream_of, to_device
 
-_pool = _lib.WorkspacePool()
+def plan(N: int, K: int, M: int) -> dict:
+    """The launch plan the kernel uses for a shape (strip width, cluster K split, grid)."""
+    import ctypes
+    info = (ctypes.c_int32 * 8)()
+    check(lib().mb_int4_gemm_plan(N, K, M, info), "mb_int4_gemm_plan")
+    keys = ("fast", "strip", "cluster", "grid", "stages", "smem", "phases", "ntiles")
+    return dict(zip(keys, list(info)))
 
 
-def workspace_bytes(N: int, K: int, M: int) -> int:
-    return int(lib().mb_int4_gemm_workspace_size(N, K, M))
-
-
-def batched_gemm(activations, superblocks, K: int, M: int, out=None):
+def batched_gemm(activations, superblocks, K: int, M: int, out=None, dev_err=None):
     """fp16 ``[N, K] x int4[K, M] -> fp16 [N, M]`` with fp32 accumulation.
 
     activations: fp16 ``[N, K]`` (NumPy or torch CUDA); superblocks: uint8
     ``[K*M/256*144]`` super-block stream on the same device (or NumPy); ``out``:
-    optional fp16 ``[N, M]`` CUDA tensor to write into.
+    optional fp16 ``[N, M]`` CUDA tensor to write into; ``dev_err``: optional int32
+    CUDA tensor whose first word receives device error bits (bounded waits).
     """
     t = _lib.torch()
     a, was_np = to_device(activations, t.float16)
@@ -50,26 +53,11 @@ def batched_gemm(activations, superblocks, K: int, M: int, out=None):
         out = t.empty((N, M), dtype=t.float16, device=a.device)
     elif out.shape != (N, M) or out.dtype != t.float16 or not out.is_contiguous():
         raise ValueError("out must be a contiguous fp16 [N, M] tensor")
-    st = stream_of(a.device)
-    nbytes = workspace_bytes(N, K, M)
-    ws = _pool.get(a.device, st, nbytes)
-    check(lib().mb_int4_gemm(ptr(a), ptr(sb), ptr(out), N, K, M, ptr(ws), ws.numel(), st), "mb_int4_gemm")
+    check(lib().mb_int4_gemm(ptr(a), ptr(sb), ptr(out), N, K, M, ptr(dev_err) if dev_err is not None else None,
+                             stream_of(a.device)), "mb_int4_gemm")
     if was_np:
         return out.cpu().numpy()
     return out
-
-
-def device_status(device=None) -> int:
-    """Read and clear the device error word of this stream's GEMM workspace
-    (non-zero means a bounded wait inside the kernel gave up)."""
-    import ctypes
-    t = _lib.torch()
-    dev = device or t.device("cuda", t.cuda.current_device())
-    st = stream_of(dev)
-    ws = _pool.get(dev, st, 256)
-    v = ctypes.c_uint32(0)
-    check(lib().mb_int4_gemm_device_status(ptr(ws), ctypes.byref(v), st), "mb_int4_gemm_device_status")
-    return int(v.value)
 
 
 def gemm_bytes(N: int, K: int, M: int) -> int:
@@ -81,6 +69,6 @@ def gemm_flops(N: int, K: int, M: int) -> int:
     return 2 * N * K * M
 
 
-__all__ = ["batched_gemm", "workspace_bytes", "device_status", "gemm_bytes", "gemm_flops"]
+__all__ = ["batched_gemm", "plan", "gemm_bytes", "gemm_flops"]
 
 _ = np  # numpy inputs are accepted through to_device

@@ -5,7 +5,9 @@ Tolerance: the north-star bar is 1e-2 relative with fp32 accumulation
 (``rtol = atol = 1e-2`` as in antigravity-engine/tests/test_batched_speed.py:66-70).
 The kernel multiplies exactly the same fp16 weights (bit-exact dequant) and fp16
 activations in fp32, only the summation order differs, so it is also held to a much
-tighter bar: relative L2 error <= 1e-3 and every element within 2 fp16 ulps.
+tighter bar: relative L2 error <= 1e-3 and every element within 2 fp16 ulps plus an
+absolute floor of 1e-4 x max|ref| (fp32 summation-order noise where a result
+cancels to near zero).
 """
 
 import numpy as np
@@ -24,7 +26,8 @@ def close(got, ref):
     rel = np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-30)
     assert rel <= 1e-3, f"relative L2 error {rel:.3e}"
     ulp = np.spacing(np.abs(ref).astype(np.float16)).astype(np.float32)
-    assert np.all(np.abs(g - r) <= 2 * ulp + 1e-6), f"max ulp err {np.max(np.abs(g - r) / ulp):.2f}"
+    floor = 1e-4 * float(np.max(np.abs(r))) if r.size else 0.0
+    assert np.all(np.abs(g - r) <= 2 * ulp + floor), f"max ulp err {np.max((np.abs(g - r) - floor) / ulp):.2f}"
 
 
 def run(x, st, K, M):
@@ -97,21 +100,22 @@ def test_metal_known_answers(cuda):
     assert not np.any(np.isnan(y)) and not np.any(np.isinf(y))
 
 
-def test_repeated_calls_keep_workspace_clean(cuda):
-    """The split-K workspace is re-zeroed by every call: 20 back-to-back calls on the
-    same stream give identical results and the device error word stays 0."""
+@pytest.mark.parametrize("N", [1, 8, 16, 32])
+def test_repeated_calls_are_deterministic(cuda, N):
+    """The split-K partial sums are reduced in a fixed order on chip: 20 back-to-back
+    calls on one stream give bit-identical results and the device error word stays 0."""
     import torch
-    from moat_b200.gemm import batched_gemm, device_status
-    K, M, N = 3072, 8192, 16
+    from moat_b200.gemm import batched_gemm
+    K, M = 3072, 8192
     st = torch.from_numpy(O.quantize_pack_matrix(O.make_weights(K, M, 5))).cuda()
     x = torch.from_numpy(O.make_activations(N, K, 5)).cuda()
-    first = batched_gemm(x, st, K, M).clone()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    first = batched_gemm(x, st, K, M, dev_err=err).clone()
     for _ in range(20):
-        y = batched_gemm(x, st, K, M)
+        y = batched_gemm(x, st, K, M, dev_err=err)
     torch.cuda.synchronize()
-    diff = (y.float() - first.float()).abs().max().item()
-    assert diff <= 2e-3 * first.float().abs().max().item()
-    assert device_status() == 0
+    assert torch.equal(y, first)
+    assert int(err.item()) == 0
 
 
 def test_numpy_host_inputs_end_to_end(cuda):
