@@ -337,8 +337,10 @@ def run_moat(args):
     peak, peak_kind = load_peaks()
     traffic = load_traffic()
     tr = None
-    if traffic and "k_gemm_tma" in traffic:
-        tr = traffic["k_gemm_tma"].get("dram_bytes_per_launch_sweep_avg")
+    if traffic and "k_gemm_int4" in traffic:
+        per = traffic["k_gemm_int4"].get("dram_bytes_per_launch", {})
+        if all(str(n) in per for n in sweep) and world == 1:
+            tr = sum(per[str(n)] for n in sweep) / len(sweep)
 
     if rank == 0:
         cpu = None if (world > 1 or args.no_cpu) else cpu_reference(budget_s=args.cpu_seconds)
@@ -356,7 +358,7 @@ def run_moat(args):
             "tok_per_s": tok_per_s,
             "per_n": per_n,
             "plans": {str(n): plans[n] for n in sweep},
-            "roofline": {"bound": "hbm", "kernel": "k_gemm_tma", "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": "k_gemm_int4", "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": tr, "bytes_per_launch": "K*M*144/256 + 2NK + 2NM (this rank's shard)"},
             "gpu_launches": args.steps * R * len(sweep),

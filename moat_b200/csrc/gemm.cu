@@ -48,7 +48,7 @@ constexpr int kMaxCk = 8;
 //  (M % 256 == 128) rows of each phase are stored together.
 template <int WS, int P>
 struct Layout {
-  static_assert(WS == 256 || WS == 128 || WS == 64, "strip width");
+  static_assert(WS == 256 || WS == 128, "strip width");
   static_assert(WS != 256 || P == 1, "a 256-wide strip needs M % 256 == 0");
   static_assert(P == 1 || P == 2, "row phases");
   static constexpr int kNibRow = (WS == 128) ? (P == 1 ? 80 : 96) : (P == 1 ? 48 : 32);

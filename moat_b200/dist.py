@@ -68,8 +68,10 @@ def gather_columns(local, bounds: Sequence[Tuple[int, int]], group=None):
     else:
         send = torch.zeros((N, wmax), dtype=local.dtype, device=local.device)
         send[:, :local.shape[1]] = local
-    recv = torch.empty((world, N, wmax), dtype=local.dtype, device=local.device)
+    # flat [world * N, wmax] receive buffer: the layout every backend accepts
+    recv = torch.empty((world * N, wmax), dtype=local.dtype, device=local.device)
     dist.all_gather_into_tensor(recv, send, group=group)
+    recv = recv.view(world, N, wmax)
     M = bounds[-1][1]
     if all(c1 - c0 == wmax for c0, c1 in bounds):
         return recv.permute(1, 0, 2).reshape(N, M)
@@ -91,8 +93,9 @@ def gather_heads(local, bounds: Sequence[Tuple[int, int]], group=None):
     if local.shape[1] != hmax:
         send = torch.zeros((T, hmax, d), dtype=local.dtype, device=local.device)
         send[:, :local.shape[1]] = local
-    recv = torch.empty((world, T, hmax, d), dtype=local.dtype, device=local.device)
+    recv = torch.empty((world * T, hmax, d), dtype=local.dtype, device=local.device)
     dist.all_gather_into_tensor(recv, send, group=group)
+    recv = recv.view(world, T, hmax, d)
     H = bounds[-1][1]
     out = torch.empty((T, H, d), dtype=local.dtype, device=local.device)
     for r, (h0, h1) in enumerate(bounds):
