@@ -248,19 +248,15 @@ def run_moat(args):
 
     stream = torch.cuda.Stream(device=dev)
     plans = {n: plan(n, K, Ms) for n in sweep}
-    # stream-K workspace (zeroed once; every call leaves it ready for the next)
-    wsn = max([L.mb_int4_gemm_workspace_size(n, K, Ms) for n in sweep] + [256])
-    ws = torch.zeros(wsn, dtype=torch.uint8, device=dev)
 
     def gemm_launches(n):
         st = stream.cuda_stream
         x = xs[n]
         y = ys[n]
         for r in range(R):
-            rc = L.mb_int4_gemm_ws(x.data_ptr(), ring[r].data_ptr(), y[r].data_ptr(), n, K, Ms, ws.data_ptr(), wsn,
-                                   None, st)
+            rc = L.mb_int4_gemm(x.data_ptr(), ring[r].data_ptr(), y[r].data_ptr(), n, K, Ms, None, st)
             if rc != 0:
-                raise RuntimeError(f"mb_int4_gemm_ws failed: {rc}")
+                raise RuntimeError(f"mb_int4_gemm failed: {rc}")
 
     torch.cuda.synchronize()
     graphs = {}

@@ -111,26 +111,11 @@ int32_t mb_lut_gather_f16(const int32_t* idx, int64_t n, const uint16_t* lut, in
 int32_t mb_int4_gemm(const uint16_t* act, const uint8_t* sb, uint16_t* out, int32_t N, int32_t K, int32_t M,
                      uint32_t* dev_err, void* stream);
 
-/* Workspace bytes of mb_int4_gemm_ws for this shape (0: the stream-K path does not
- * apply and no workspace is needed). No counterpart in the reference (its GEMM runs
- * inside a context that owns its buffers). */
-size_t mb_int4_gemm_workspace_size(int32_t N, int32_t K, int32_t M);
-
-/* mb_int4_gemm with a caller-owned device workspace (256-byte aligned, >=
- * mb_int4_gemm_workspace_size bytes, zero-filled once before its first use; every
- * call leaves it ready for the next). With it, batches of up to 16 rows (per 32-row block) run
- * the stream-K kernel: one CTA per SM, partial tiles summed in a fixed order
- * (deterministic). Calls that share a workspace must be ordered (same stream). */
-int32_t mb_int4_gemm_ws(const uint16_t* act, const uint8_t* sb, uint16_t* out, int32_t N, int32_t K, int32_t M,
-                        void* workspace, size_t workspace_bytes, uint32_t* dev_err, void* stream);
-
 /* Launch plan of the first 32-row block for a shape (introspection, no reference
- * counterpart). info must hold 8 int32. info[0]: 3 stream-K (used by
- * mb_int4_gemm_ws, N <= 8), 2 tensor-core (tcgen05, 16 < N <= 32), 1 cluster
- * kernel, 0 generic. [1] strip width, [2] CTAs per cluster, [3] grid size, [4]
- * pipeline stages, [5] dynamic shared memory bytes; [6], [7]: workspace slots per
- * strip and 8-row batch tiles (3), TMEM columns and MMA N (2), row phases and
- * 8-row batch tiles (1). */
+ * counterpart). info must hold 8 int32. info[0]: 2 tensor-core (tcgen05,
+ * 16 < N <= 32), 1 cluster kernel, 0 generic. [1] strip width, [2] CTAs per
+ * cluster, [3] grid size, [4] pipeline stages, [5] dynamic shared memory bytes;
+ * [6], [7]: TMEM columns and MMA N (2), row phases and 8-row batch tiles (1). */
 int32_t mb_int4_gemm_plan(int32_t N, int32_t K, int32_t M, int32_t* info);
 
 /* Columns [c0, c1) of a packed [K, M] weight, re-packed as its own [K, c1-c0]

@@ -202,6 +202,10 @@ __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ void st_shared_cluster_v2(uint32_t addr, float a, float b) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+
 // 3-D tiled TMA load (global -> this CTA's shared memory), completion on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
                                             uint64_t policy) {

@@ -18,9 +18,7 @@ from __future__ import annotations
 import numpy as np
 
 from . import _lib
-from ._lib import WorkspacePool, check, lib, ptr, stream_of, to_device
-
-_WS = WorkspacePool()  # per (device, stream) zeroed workspace for the stream-K kernel
+from ._lib import check, lib, ptr, stream_of, to_device
 
 def plan(N: int, K: int, M: int) -> dict:
     """The launch plan the kernel uses for a shape (strip width, cluster K split, grid)."""
@@ -55,12 +53,8 @@ def batched_gemm(activations, superblocks, K: int, M: int, out=None, dev_err=Non
         out = t.empty((N, M), dtype=t.float16, device=a.device)
     elif out.shape != (N, M) or out.dtype != t.float16 or not out.is_contiguous():
         raise ValueError("out must be a contiguous fp16 [N, M] tensor")
-    stream = stream_of(a.device)
-    need = lib().mb_int4_gemm_workspace_size(N, K, M)
-    ws = _WS.get(a.device, stream, need) if need else None
-    check(lib().mb_int4_gemm_ws(ptr(a), ptr(sb), ptr(out), N, K, M, ptr(ws) if ws is not None else None,
-                                ws.numel() if ws is not None else 0, ptr(dev_err) if dev_err is not None else None,
-                                stream), "mb_int4_gemm_ws")
+    check(lib().mb_int4_gemm(ptr(a), ptr(sb), ptr(out), N, K, M, ptr(dev_err) if dev_err is not None else None,
+                             stream_of(a.device)), "mb_int4_gemm")
     if was_np:
         return out.cpu().numpy()
     return out

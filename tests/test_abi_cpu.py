@@ -42,46 +42,34 @@ def test_binding_covers_only_declared(L):
 
 def test_gemm_plans(L):
     """Host-side planning of the GEMM launch for the BASELINE shapes; needs no GPU
-    (148 SMs assumed when none is visible). Kinds: 3 stream-K, 2 tensor-core,
-    1 cluster kernel, 0 generic."""
+    (148 SMs assumed when none is visible). Kinds: 2 tensor-core, 1 cluster kernel,
+    0 generic."""
     info = (ctypes.c_int32 * 8)()
     for (N, K, M) in [(8, 2048, 2048), (1, 3072, 8192), (32, 3072, 8192), (16, 2048, 5504), (16, 2048, 151936),
                       (16, 5504, 2048), (24, 3072, 8192)]:
         assert L.mb_int4_gemm_plan(N, K, M, info) == 0
         kind, strip, ck, grid, stages, smem = list(info)[:6]
-        assert kind in (1, 2, 3), (N, K, M)
+        assert kind in (1, 2), (N, K, M)
         assert smem <= 227 * 1024 and stages >= 1
-        if kind == 3:  # stream-K: one CTA per SM, 256-column strips
-            assert N <= 8 and M % 256 == 0 and strip == 256 and 1 <= grid <= 148
-            assert L.mb_int4_gemm_workspace_size(N, K, M) > 0
-        elif kind == 2:
+        if kind == 2:
             assert 16 < N <= 32 and M % 256 == 0 and info[6] in (128, 256) and info[7] in (16, 32)
             assert grid == (M // 256) * ck and grid <= 148
         else:
             assert strip in (128, 256) and M % strip == 0 and 1 <= ck <= 8
             assert grid == (M // strip) * ck and (ck == 1 or grid <= 148)
     assert L.mb_int4_gemm_plan(8, 12, 64, info) == 0 and info[0] == 0  # generic path
-    assert L.mb_int4_gemm_workspace_size(8, 12, 64) == 0
 
 
-def test_stream_k_partition():
-    """The stream-K split the kernel uses (CTA c owns slices [c U / G, (c+1) U / G),
-    strip s's partial tiles come from CTAs owner(s KS) .. owner(s KS + KS - 1) with
-    owner(x) = ((x + 1) G - 1) // U) covers every slice once and fits the slots."""
-    for (K, M, G) in [(3072, 8192, 148), (2048, 2048, 148), (2048, 151936, 148), (256, 512, 148), (4104, 256, 148),
-                      (3072, 8192, 37), (16, 256, 148)]:
-        KS, strips = (K + 15) // 16, M // 256
-        U = strips * KS
-        G = min(G, U)
-        b = [c * U // G for c in range(G + 1)]
-        assert b[0] == 0 and b[-1] == U and all(b[i] < b[i + 1] for i in range(G))
-        per = U // G
-        maxP = min(G, KS // max(per, 1) + 2)
-        for s in range(strips):
-            x0, x1 = s * KS, s * KS + KS - 1
-            cf, cl = ((x0 + 1) * G - 1) // U, ((x1 + 1) * G - 1) // U
-            assert b[cf] <= x0 < b[cf + 1] and b[cl] <= x1 < b[cl + 1]
-            assert cl - cf + 1 <= maxP
+def test_cluster_owner_ranges():
+    """The cluster kernel's final reduction gives CTA q of a Ck-CTA cluster the strip
+    columns [q cw, min((q + 1) cw, WS)) with cw = ceil(WS / Ck) rounded up to even:
+    every column has an owner rank < Ck and the ranges cover the strip exactly (the
+    planner may pick any Ck from 1 to 8)."""
+    for WS in (128, 256):
+        for Ck in range(1, 9):
+            cw = ((WS + Ck - 1) // Ck + 1) & ~1
+            assert max(col // cw for col in range(0, WS, 2)) < Ck
+            assert sum(max(0, min(cw, WS - q * cw)) for q in range(Ck)) == WS
 
 
 def test_version_and_status_strings(L):

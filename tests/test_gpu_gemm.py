@@ -127,32 +127,3 @@ def test_numpy_host_inputs_end_to_end(cuda):
     assert isinstance(y, np.ndarray) and y.dtype == np.float16 and y.shape == (N, M)
     close(y, O.gemm(x, O.unpack_superblock_weights(st).reshape(K, M)))
 
-
-@pytest.mark.parametrize("N", [1, 8, 16, 24])
-def test_workspace_and_plain_entry_points_agree(cuda, N):
-    """mb_int4_gemm_ws (stream-K with a workspace) and mb_int4_gemm (no workspace)
-    both match the oracle; the workspace's arrival counters (its first 4 bytes per
-    256-column strip) are zero again after every call."""
-    import torch
-    from moat_b200._lib import lib
-    K, M = 3072, 8192
-    st = O.quantize_pack_matrix(O.make_weights(K, M, 77))
-    w = O.unpack_superblock_weights(st).reshape(K, M)
-    x = O.make_activations(N, K, 3)
-    ref = O.gemm(x, w)
-    xd, sd = torch.from_numpy(x).cuda(), torch.from_numpy(st).cuda()
-    need = lib().mb_int4_gemm_workspace_size(N, K, M)
-    ws = torch.zeros(max(need, 256), dtype=torch.uint8, device="cuda")
-    err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    stream = torch.cuda.current_stream().cuda_stream
-    for use_ws in (True, False, True):
-        y = torch.empty((N, M), dtype=torch.float16, device="cuda")
-        if use_ws:
-            rc = lib().mb_int4_gemm_ws(xd.data_ptr(), sd.data_ptr(), y.data_ptr(), N, K, M, ws.data_ptr(), ws.numel(),
-                                       err.data_ptr(), stream)
-        else:
-            rc = lib().mb_int4_gemm(xd.data_ptr(), sd.data_ptr(), y.data_ptr(), N, K, M, err.data_ptr(), stream)
-        assert rc == 0
-        close(y.cpu().numpy(), ref)
-        assert int(err.item()) == 0
-        assert int(ws[: (M // 256) * 4].count_nonzero().item()) == 0
