@@ -200,11 +200,11 @@ struct RunCols {
 };
 
 // NT: n-tiles of 8 batch rows (1, 2, 4); WS: strip width; P: row phases (1, 2);
-// CW: consumer warps. __launch_bounds__(.., 2): a CTA uses at most half an SM's
-// registers so the next call's CTAs (launched early through PDL) can be resident
-// and prefetch their weights while this one computes.
-template <int NT, int WS, int P, int CW>
-__global__ void __launch_bounds__((CW + 1) * 32, 2)
+// CW: consumer warps; MINB: CTAs per SM the plan wants resident -- 2 leaves room for
+// the next call's CTA (launched early through PDL) to prefetch, 1 gives a CTA that
+// has the SM to itself the registers for a deeper instruction schedule.
+template <int NT, int WS, int P, int CW, int MINB>
+__global__ void __launch_bounds__((CW + 1) * 32, MINB)
     k_gemm_int4(const __grid_constant__ WMaps maps, const GemmParams p) {
   using L = Layout<WS, P>;
   constexpr int MR = RunCols<NT, WS>::v;  // columns per thread run
@@ -432,6 +432,7 @@ __global__ void __launch_bounds__(128) k_gemm_generic(const uint16_t* __restrict
 struct Plan {
   int ws = 0, P = 1, Ck = 1, nt = 1, S = 0, smem = 0, xstride = 0, xbytes = 0, ctas = 0, slotoff = 0;
   bool fast = false;
+  bool solo = false;  // one CTA per SM
 };
 
 static constexpr int kCW = 8;                   // consumer warps per CTA
@@ -508,17 +509,17 @@ static Plan plan_gemm(int N, int K, int M, int sms) {
   // 116 KB), since two CTAs of one call on an SM take twice as long and hold back the
   // whole call. A small share is dominated by start-up latency: leave room for the next
   // call's CTA to start early (programmatic dependent launch) and prefetch.
-  if (static_cast<long long>(pl.ws) * ((KS + pl.Ck - 1) / pl.Ck) * kSliceRows >= 64 * 1024)
-    pl.smem = std::max(pl.smem, 116 * 1024);
+  pl.solo = static_cast<long long>(pl.ws) * ((KS + pl.Ck - 1) / pl.Ck) * kSliceRows >= 64 * 1024;
+  if (pl.solo) pl.smem = std::max(pl.smem, 116 * 1024);
   pl.fast = true;
   return pl;
 }
 
-template <int NT, int WS, int P>
+template <int NT, int WS, int P, int MINB>
 static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M,
                        uint32_t* err, cudaStream_t st) {
   using L = Layout<WS, P>;
-  auto kern = k_gemm_int4<NT, WS, P, kCW>;
+  auto kern = k_gemm_int4<NT, WS, P, kCW, MINB>;
   static bool attr_set[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MB_ERR_LAUNCH;
@@ -582,14 +583,21 @@ static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, u
   return launch_status();
 }
 
+template <int NT, int MINB>
+static int dispatch_fast_b(const Plan& pl, const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M,
+                           uint32_t* err, cudaStream_t st) {
+  if (pl.ws == 256) return launch_fast<NT, 256, 1, MINB>(pl, act, sb, out, N, K, M, err, st);
+  if (pl.ws == 128)
+    return pl.P == 1 ? launch_fast<NT, 128, 1, MINB>(pl, act, sb, out, N, K, M, err, st)
+                     : launch_fast<NT, 128, 2, MINB>(pl, act, sb, out, N, K, M, err, st);
+  return MB_ERR_UNSUPPORTED;
+}
+
 template <int NT>
 static int dispatch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M,
                          uint32_t* err, cudaStream_t st) {
-  if (pl.ws == 256) return launch_fast<NT, 256, 1>(pl, act, sb, out, N, K, M, err, st);
-  if (pl.ws == 128)
-    return pl.P == 1 ? launch_fast<NT, 128, 1>(pl, act, sb, out, N, K, M, err, st)
-                     : launch_fast<NT, 128, 2>(pl, act, sb, out, N, K, M, err, st);
-  return MB_ERR_UNSUPPORTED;
+  return pl.solo ? dispatch_fast_b<NT, 1>(pl, act, sb, out, N, K, M, err, st)
+                 : dispatch_fast_b<NT, 2>(pl, act, sb, out, N, K, M, err, st);
 }
 
 static int launch_generic(const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M, cudaStream_t st) {
