@@ -112,10 +112,9 @@ int32_t mb_int4_gemm(const uint16_t* act, const uint8_t* sb, uint16_t* out, int3
                      uint32_t* dev_err, void* stream);
 
 /* Launch plan of the first 32-row block for a shape (introspection, no reference
- * counterpart). info must hold 8 int32. info[0]: 2 tensor-core (tcgen05,
- * 16 < N <= 32), 1 cluster kernel, 0 generic. [1] strip width, [2] CTAs per
- * cluster, [3] grid size, [4] pipeline stages, [5] dynamic shared memory bytes;
- * [6], [7]: TMEM columns and MMA N (2), row phases and 8-row batch tiles (1). */
+ * counterpart). info must hold 8 int32: [0] fast path (1) or generic (0), [1] strip
+ * width, [2] CTAs per cluster (K split), [3] grid size, [4] pipeline stages, [5]
+ * dynamic shared memory bytes, [6] row phases, [7] 8-row batch tiles. */
 int32_t mb_int4_gemm_plan(int32_t N, int32_t K, int32_t M, int32_t* info);
 
 /* Columns [c0, c1) of a packed [K, M] weight, re-packed as its own [K, c1-c0]

@@ -30,7 +30,6 @@
 #include <algorithm>
 
 #include "common.cuh"
-#include "gemm_tc.cuh"
 
 namespace mb {
 
@@ -611,13 +610,10 @@ static int launch_generic(const uint16_t* act, const uint8_t* sb, uint16_t* out,
   return launch_status();
 }
 
-// One launch over up to 32 batch rows: the tensor-core path for 16 < N <= 32, else
-// the cluster kernel, else the generic one.
+// One launch over up to 32 batch rows: the cluster kernel, else the generic one.
 static int gemm_rows(const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M, uint32_t* err,
                      cudaStream_t st) {
   if (aligned(act, 16) && aligned(sb, 16) && aligned(out, 4)) {
-    tc::TcPlan tp;
-    if (N > 16 && tc::plan(N, K, M, sm_count(), &tp)) return tc::launch(tp, act, sb, out, N, K, M, err, st);
     const Plan pl = plan_gemm(N, K, M, sm_count());
     if (pl.fast) {
       if (pl.nt == 1) return dispatch_fast<1>(pl, act, sb, out, N, K, M, err, st);
@@ -656,18 +652,6 @@ int32_t mb_int4_gemm(const uint16_t* act, const uint8_t* sb, uint16_t* out, int3
 int32_t mb_int4_gemm_plan(int32_t N, int32_t K, int32_t M, int32_t* info) {
   if (!info) return MB_ERR_NULL;
   if (N < 1 || K < 1 || M < 1) return MB_ERR_ARGS;
-  tc::TcPlan tp;
-  if (std::min(N, 32) > 16 && tc::plan(std::min(N, 32), K, M, sm_count(), &tp)) {  // tensor-core path
-    info[0] = 2;
-    info[1] = 256;
-    info[2] = tp.Ck;
-    info[3] = tp.ctas;
-    info[4] = tp.S;
-    info[5] = tp.smem;
-    info[6] = tp.tcols;
-    info[7] = tp.NP;
-    return MB_OK;
-  }
   const Plan pl = plan_gemm(std::min(N, 32), K, M, sm_count());
   info[0] = pl.fast ? 1 : 0;
   info[1] = pl.ws;

@@ -42,21 +42,16 @@ def test_binding_covers_only_declared(L):
 
 def test_gemm_plans(L):
     """Host-side planning of the GEMM launch for the BASELINE shapes; needs no GPU
-    (148 SMs assumed when none is visible). Kinds: 2 tensor-core, 1 cluster kernel,
-    0 generic."""
+    (148 SMs assumed when none is visible)."""
     info = (ctypes.c_int32 * 8)()
     for (N, K, M) in [(8, 2048, 2048), (1, 3072, 8192), (32, 3072, 8192), (16, 2048, 5504), (16, 2048, 151936),
                       (16, 5504, 2048), (24, 3072, 8192)]:
         assert L.mb_int4_gemm_plan(N, K, M, info) == 0
         kind, strip, ck, grid, stages, smem = list(info)[:6]
-        assert kind in (1, 2), (N, K, M)
+        assert kind == 1, (N, K, M)
         assert smem <= 227 * 1024 and stages >= 1
-        if kind == 2:
-            assert 16 < N <= 32 and M % 256 == 0 and info[6] in (128, 256) and info[7] in (16, 32)
-            assert grid == (M // 256) * ck and grid <= 148
-        else:
-            assert strip in (128, 256) and M % strip == 0 and 1 <= ck <= 8
-            assert grid == (M // strip) * ck and (ck == 1 or grid <= 148)
+        assert strip in (128, 256) and M % strip == 0 and 1 <= ck <= 8
+        assert grid == (M // strip) * ck and (ck == 1 or grid <= 148)
     assert L.mb_int4_gemm_plan(8, 12, 64, info) == 0 and info[0] == 0  # generic path
 
 
