@@ -152,6 +152,23 @@ int32_t mb_decode_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
                        int32_t H, int32_t L, int32_t d, float scale, const uint16_t* table, int32_t size,
                        float range_max, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode attention exactly as mb_decode_attn, on a fixed per-device scratch of
+ * MB_ATTN_NOALLOC_SCRATCH_BYTES that belongs to the library: the call allocates and
+ * frees no device memory. No counterpart in the reference (its attention runs on the
+ * host); it serves callers that cannot provide a workspace, such as a binding with no
+ * device allocator or a process whose caching allocator already holds the free HBM.
+ *   - returns MB_ERR_WORKSPACE, launching nothing, when
+ *     mb_decode_attn_workspace_size(T, H, L, d) > MB_ATTN_NOALLOC_SCRATCH_BYTES;
+ *   - the scratch needs no zeroing: the kernels write every scratch byte they read;
+ *   - all calls on one device share the scratch: calls that may overlap (unordered
+ *     streams, several host threads) race and can return wrong outputs;
+ *   - the first call on each device looks up the scratch address with that device
+ *     current; make it before any stream capture begins on that device. */
+#define MB_ATTN_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+int32_t mb_decode_attn_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int32_t T,
+                               int32_t H, int32_t L, int32_t d, float scale, const uint16_t* table, int32_t size,
+                               float range_max, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,6 +35,8 @@ SIGNATURES = {
     "mb_decode_attn_workspace_size": (_c_sz, [_c_i32, _c_i32, _c_i32, _c_i32]),
     "mb_decode_attn": (_c_i32, [_vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _c_f, _vp, _c_i32, _c_f,
                                 _vp, _c_sz, _vp]),
+    "mb_decode_attn_noalloc": (_c_i32, [_vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _c_f, _vp, _c_i32,
+                                        _c_f, _vp]),
 }
 
 _lock = threading.Lock()

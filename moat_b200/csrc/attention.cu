@@ -260,6 +260,25 @@ static AttnWs carve_attn_ws(void* base, int T, int H, int L, int d, int C, size_
   return w;
 }
 
+// The three passes of mb_decode_attn over a scratch base that holds at least
+// mb_decode_attn_workspace_size(T, H, L, d) bytes, 256-byte aligned; arguments
+// already validated by the caller. Used by the fixed-scratch entry point
+// (attention_noalloc.cu).
+int32_t decode_attn_enqueue(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int T, int H,
+                            int L, int d, float scale, const uint16_t* table, int size, float range_max,
+                            void* scratch, cudaStream_t st) {
+  const int C = attn_chunks(L);
+  AttnWs w = carve_attn_ws(scratch, T, H, L, d, C, nullptr);
+  const float step = static_cast<float>(static_cast<double>(range_max) / (size - 1));
+  const int rows = T * H;
+  k_attn_scores<<<dim3(C, rows), kAttnBlock, 0, st>>>(q, k, L, d, C, scale, w);
+  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
+  k_attn_stats<<<rows, kAttnBlock, 0, st>>>(L, C, table, size, step, w);
+  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
+  k_attn_pv<<<dim3(C, rows), kAttnBlock, 0, st>>>(v, out, L, d, C, table, size, step, w);
+  return launch_status();
+}
+
 }  // namespace mb
 
 using namespace mb;
