@@ -188,6 +188,32 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Split form of the cluster barrier: every thread of the cluster arrives once and
+// waits once per phase (warp-convergent).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Arrival that orders nothing: for a phase whose only meaning is "this thread got here"
+// (a release would first wait for the thread's outstanding global stores).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
+// Makes this thread's generic-proxy shared-memory writes visible to the async proxy
+// (bulk copies issued after a following barrier).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from this CTA's
+// shared memory into another CTA of the cluster; `dst` and `remote_bar` are
+// shared::cluster addresses (mapa), completion is signalled on the remote mbarrier.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst, const void* src, uint32_t bytes,
+                                                  uint32_t remote_bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "r"(smem_u32(src)), "r"(bytes), "r"(remote_bar)
+      : "memory");
+}
 
 // Address of the same shared-memory location in CTA `rank` of this cluster.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t local_addr, uint32_t rank) {

@@ -16,14 +16,18 @@
 //  * One producer thread per CTA streams the strip's super-block rows with 3-D TMA
 //    tile loads (cp.async.bulk.tensor, L2 evict-first) into a ring of shared-memory
 //    stages guarded by mbarriers. The weights never depend on the previous kernel,
-//    so the whole ring is filled before griddepcontrol.wait (programmatic dependent
-//    launch): a CTA of the next call, resident beside this one, prefetches while this
-//    one computes.
-//  * After griddepcontrol.wait the consumer warps stage the CTA's activation slice in
-//    shared memory (one pass, L2 resident) and expand nibbles straight into
-//    mma.m16n8k16 A fragments in registers: byte permute + magic-exponent fp16
-//    conversion + one fp16 multiply by the group scale, bit-exact with the reference
-//    dequant; the batch (padded to 8/16/32) is the MMA n dimension, fp32 accumulate.
+//    so the ring is filled before griddepcontrol.wait (programmatic dependent
+//    launch). After it the consumer warps copy the CTA's activation slice (L2
+//    resident) into shared memory with all loads of a round in flight.
+//  * Consumer warps expand nibbles straight into mma.m16n8k16 A fragments in
+//    registers: byte permute + magic-exponent fp16 conversion + one fp16 multiply by
+//    the group scale, bit-exact with the reference dequant; the batch (padded to
+//    8/16/32) is the MMA n dimension, fp32 accumulate.
+//  * Reduction: the k-group warps park their partial tiles in the drained ring and sum
+//    them in a fixed order into a send tile holding one block per owner CTA of the
+//    cluster; one bulk shared-memory copy per peer (cp.async.bulk.shared::cluster)
+//    moves each block, completion counted on the owner's mbarrier, and each owner adds
+//    the Ck blocks of its columns in rank order.
 //  * Shared-memory rows are laid out so the fragment loads are bank-conflict free:
 //    full 144-byte super-block rows (WS = 256), or a 16-byte scale row plus a
 //    nibble row padded to 80 / 96 bytes by the TMA box (WS = 128, M % 256 == 128).
@@ -39,6 +43,7 @@ constexpr int kSPS = 8;         // slices per full stage (128 rows)
 constexpr int kStageRows = kSPS * kSliceRows;
 constexpr int kMaxStages = 8;
 constexpr int kMaxCk = 8;
+constexpr int kAhead = 3;  // weight stages in flight per CTA
 
 // Shared-memory layout of one pipeline stage (128 rows of the CTA's strip).
 //  WS = 256: full 144-byte super-block rows (scales then nibbles), row stride 144 B.
@@ -75,13 +80,29 @@ struct GemmParams {
   int KS;               // k slices (ceil(K / 16))
   int Ck;               // CTAs per cluster = K split
   int S;                // stages in the ring
-  int xstride;          // bytes per activation row in shared memory
-  int xbytes;           // activation region
-  int slotoff;          // receive slots of the cluster reduction (outside the stage ring)
+  int xchunks;          // 128-wide k chunks of the activation slice
+  int xcstride;         // bytes per chunk in shared memory (N rows of kXRow bytes, 128-aligned)
+  int sendoff;          // byte offset of the send tile [Ck][N][cwp] (reuses ring + activations)
+  int baroff;           // byte offset of the mbarriers
+  int recvoff;          // byte offset of the receive slots [Ck][N][cwp] (outside the ring)
 };
+
+// Activations in shared memory: chunks of 128 k values by N rows; a row takes 272
+// bytes (128 values + 8 pad), so consecutive rows start 4 banks apart and the
+// B-fragment loads are conflict free.
+constexpr int kXChunk = 128;
+constexpr int kXRow = 272;
 
 struct WMaps {  // weight tensor maps: full-stage and 16-row boxes (scale / nibble rows)
   CUtensorMap full_a, full_b, slice_a, slice_b;
+};
+
+// Row stride (floats) of a k-group parking tile: WS columns with 2 pad floats after
+// every MR-column run, and a stride of 4 (mod 16) between batch rows, so the float2
+// stores of a warp's fragments hit distinct banks for MR = 32, 16 and 8.
+template <int WS, int MR>
+struct ParkRow {
+  static constexpr int v = (WS + 2 * WS / MR - 4 + 15) / 16 * 16 + 4;
 };
 
 template <int NW>
@@ -211,16 +232,16 @@ __global__ void __launch_bounds__((CW + 1) * 32, MINB)
   constexpr int kCm = WS / (8 * MR);      // column parts per strip (one warp each)
   constexpr int kKG = CW / kCm;           // warps sharing a column part (k groups)
   static_assert(kCm * kKG == CW, "warp layout");
-  constexpr int kThreads = (CW + 1) * 32;
-  // row stride (floats) of the k-group parking tile: WS columns, one pad per 32, and a
-  // stride of 4 (mod 16) between batch rows
-  constexpr int kRow = (WS + WS / 32 + 12) / 16 * 16 + 4;
+  constexpr int kRow = ParkRow<WS, MR>::v;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base, derived from the shared array itself so that every access
+  // below compiles to a shared-memory (not generic) load or store
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* stages = smem;
   uint8_t* xs = stages + p.S * L::kStageBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(xs + p.xbytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.baroff);
   uint64_t* empty = full + kMaxStages;
+  uint64_t* rbar = empty + kMaxStages;  // the peers' partial sums of this CTA's columns landed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int strip = blockIdx.x / p.Ck;
@@ -229,6 +250,12 @@ __global__ void __launch_bounds__((CW + 1) * 32, MINB)
   const int sl1 = static_cast<int>((static_cast<long long>(q + 1) * p.KS) / p.Ck);
   const int nst = (sl1 - sl0 + kSPS - 1) / kSPS;
   const int c0 = strip * WS;
+  // CTA q of the cluster owns columns [q cw, min((q + 1) cw, WS)) of the strip:
+  // ceil(WS / Ck) rounded up to even, so col / cw < Ck for every column. Partial sums
+  // travel in blocks of N rows x cwp floats (a multiple of 16 bytes).
+  const int cw = ((WS + p.Ck - 1) / p.Ck + 1) & ~1;
+  const int cwp = (cw + 3) & ~3;
+  const uint32_t blk = static_cast<uint32_t>(p.N * cwp * 4);
   // per row phase: super-block index within a period (y), first nibble byte of the
   // strip in that super-block (x) and the scale index of the strip's first column
   int ey[P], ex[P], grp[P];
@@ -246,17 +273,31 @@ __global__ void __launch_bounds__((CW + 1) * 32, MINB)
       mbar_init(full + s, 1);
       mbar_init(empty + s, CW);
     }
+    mbar_init(rbar, 1);
     fence_mbar_init();
+    // this CTA's own arrival: the phase completes when the Ck - 1 peer blocks land
+    if (p.Ck > 1) mbar_expect_tx(rbar, static_cast<uint32_t>(p.Ck - 1) * blk);
   }
   __syncthreads();
+  if (p.Ck > 1) cluster_arrive();  // phase 0: the barriers above exist (awaited before any copy)
   pdl_launch_dependents();
 
   if (warp == CW) {
-    // ---------------- producer: weights only, no dependency on the previous grid ----
+    // ---------------- producer ----------------
     if (lane == 0) {
+      // weights never depend on the previous grid: no griddepcontrol.wait here, so the
+      // ring fills while the previous grid finishes
       const uint64_t pol = policy_evict_first();
       for (int st = 0; st < nst; ++st) {
         const int s = st % p.S;
+        // at most kAhead stages in flight: the memory system then returns this CTA's
+        // stages in order, so the first one lands early instead of with the last (with
+        // kAhead <= S the slot of stage st - kAhead is not reused yet, so its parity is
+        // unambiguous; with a shorter ring the empty wait below already implies it)
+        if (st >= kAhead && kAhead <= p.S) {
+          const int sa = st - kAhead;
+          if (!mbar_wait(full + sa % p.S, (sa / p.S) & 1) && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
+        }
         if (st >= p.S && !mbar_wait(empty + s, ((st / p.S) - 1) & 1) && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
         const int sl = sl0 + st * kSPS;
         issue_stage<WS, P>(maps, stages + s * L::kStageBytes, full + s, sl * kSliceRows, min(kSPS, sl1 - sl), ey, ex,
@@ -264,66 +305,99 @@ __global__ void __launch_bounds__((CW + 1) * 32, MINB)
       }
     }
     __syncwarp();
-  } else {
-    // ---------------- consumers ----------------
-    const int g4 = lane >> 2, t4 = lane & 3;
-    const int mpart = warp % kCm, kg = warp / kCm;
-    const int mcol = mpart * 8 * MR + g4 * MR;  // first column of this thread's run in the strip
-    const int nb = (WS == 256) ? mcol / 2 : mcol / 2;
-    const int ge = grp[0] + mcol / 32, go = grp[P - 1] + mcol / 32;
+    if (p.Ck > 1) {
+      cluster_wait();
+      cluster_arrive();
+      cluster_wait();
+    }
+    return;
+  }
 
-    pdl_wait();  // activations may come from the previous grid; all writes follow it
-    // stage this CTA's activation slice [N][k0, k1) in shared memory (zero past K)
+  // ---------------- consumers ----------------
+  const int g4 = lane >> 2, t4 = lane & 3;
+  const int mpart = warp % kCm, kg = warp / kCm;
+  const int mcol = mpart * 8 * MR + g4 * MR;  // first column of this thread's run in the strip
+  const int nb = mcol / 2;
+  const int ge = grp[0] + mcol / 32, go = grp[P - 1] + mcol / 32;
+
+  float acc[kTiles][NT][4];
+#pragma unroll
+  for (int i = 0; i < kTiles; ++i)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[i][nt][c] = 0.0f;
+  bool xok[NT];
+  const uint8_t* xbase[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int n = nt * 8 + g4;
+    xok[nt] = n < p.N;
+    xbase[nt] = xs + (xok[nt] ? n : 0) * kXRow;
+  }
+  // Activation slice -> shared memory [chunk][n][kXRow] in 16-byte pieces: thread t
+  // copies pieces t, t + T, t + 2T, ... of the [N][ppr] piece grid, kU loads in flight
+  // per round, (n, pc) advanced incrementally (no division in the loop).
+  pdl_wait();  // activations may come from the previous grid; all writes follow it
+  {
+    constexpr int T = CW * 32;
+    constexpr int kU = 8;
+    const int ppr = (sl1 - sl0) * kSliceRows / 8;  // pieces per row
+    const int pieces = p.N * ppr;
     const int k0 = sl0 * kSliceRows;
-    const int chunks = (sl1 - sl0) * kSliceRows / 8;  // 16-byte chunks per row
-    for (int idx = threadIdx.x; idx < p.N * chunks; idx += CW * 32) {
-      const int n = idx / chunks, c = idx - n * chunks;
-      const int k = k0 + c * 8;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (k < p.K) v = __ldg(reinterpret_cast<const uint4*>(p.act + static_cast<size_t>(n) * p.K + k));
-      *reinterpret_cast<uint4*>(xs + n * p.xstride + c * 16) = v;
-    }
-    named_bar_sync(1, CW * 32);
-
-    float acc[kTiles][NT][4];
+    const int dn = T / ppr, dp = T - dn * ppr;
+    int n = threadIdx.x / ppr, pc = threadIdx.x - n * ppr;
+    for (int r0 = threadIdx.x; r0 < pieces; r0 += T * kU) {
+      uint4 v[kU];
+      int so[kU];
 #pragma unroll
-    for (int i = 0; i < kTiles; ++i)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[i][nt][c] = 0.0f;
-    bool xok[NT];
-    const uint8_t* xbase[NT];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const int n = nt * 8 + g4;
-      xok[nt] = n < p.N;
-      xbase[nt] = xs + (xok[nt] ? n : 0) * p.xstride;
-    }
-
-    for (int st = 0; st < nst; ++st) {
-      const int s = st % p.S;
-      if (!mbar_wait(full + s, (st / p.S) & 1) && lane == 0 && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
-      const uint8_t* stage = stages + s * L::kStageBytes;
-      const int n = min(kSPS, sl1 - (sl0 + st * kSPS));
-      for (int j = kg; j < n; j += kKG) {
-        const int kx = (st * kSPS + j) * kSliceRows;  // k offset within the activation slice
-        const uint8_t* xr[NT];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) xr[nt] = xbase[nt] + kx * 2;
-        consume_slice<NT, WS, P, MR>(stage, j * kSliceRows + 2 * t4, nb, ge, go, xr, xok, t4, acc);
+      for (int u = 0; u < kU; ++u) {
+        v[u] = make_uint4(0u, 0u, 0u, 0u);
+        so[u] = -1;
+        if (r0 + u * T < pieces) {
+          const int k = k0 + pc * 8;
+          if (k < p.K) v[u] = __ldg(reinterpret_cast<const uint4*>(p.act + static_cast<size_t>(n) * p.K + k));
+          so[u] = (pc / (kXChunk / 8)) * p.xcstride + n * kXRow + (pc % (kXChunk / 8)) * 16;
+        }
+        pc += dp;
+        n += dn;
+        if (pc >= ppr) {
+          pc -= ppr;
+          ++n;
+        }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty + s);
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (so[u] >= 0) *reinterpret_cast<uint4*>(xs + so[u]) = v[u];
     }
+  }
+  named_bar_sync(1, CW * 32);
 
-    // park the k-group partial sums of the batch rows n < N in a padded [kKG][N][row]
-    // tile (the stage ring is drained): thread (g4, t4) holds rows 8 nt + 2 t4 + (c & 1)
-    // of columns mcol + 2 i + (c >> 1); the padding puts the 32 lanes in 32 banks
-    named_bar_sync(1, CW * 32);
-    // a run of MR <= 32 columns starting at a multiple of MR stays inside one 32-block,
-    // so all offsets below are compile-time constants from one base
-    float* rbase = reinterpret_cast<float*>(smem) + (kg * p.N + 2 * t4) * kRow + mcol + (mcol >> 5);
+  for (int st = 0; st < nst; ++st) {
+    const int s = st % p.S;
+    if (!mbar_wait(full + s, (st / p.S) & 1) && lane == 0 && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
+    const uint8_t* stage = stages + s * L::kStageBytes;
+    const int n = min(kSPS, sl1 - (sl0 + st * kSPS));
+    for (int j = kg; j < n; j += kKG) {
+      const int kx = (st * kSPS + j) * kSliceRows;  // k offset within the activation slice
+      const int xo = (kx / kXChunk) * p.xcstride + (kx % kXChunk) * 2;
+      const uint8_t* xr[NT];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) xr[nt] = xbase[nt] + xo;
+      consume_slice<NT, WS, P, MR>(stage, j * kSliceRows + 2 * t4, nb, ge, go, xr, xok, t4, acc);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + s);
+  }
+
+  // ---- k groups -> one partial tile per CTA ----
+  // Park the partial sums of the batch rows n < N in [kKG][N][kRow] (the ring and the
+  // activations are drained): thread (g4, t4) holds rows 8 nt + 2 t4 + (c & 1) of
+  // columns mcol + 2 i + (c >> 1).
+  named_bar_sync(1, CW * 32);
+  float* park = reinterpret_cast<float*>(smem);
+  {
+    float* rbase = park + (kg * p.N + 2 * t4) * kRow + mcol + 2 * (mcol / MR);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -331,54 +405,80 @@ __global__ void __launch_bounds__((CW + 1) * 32, MINB)
         if (nt * 8 + 2 * t4 + r < p.N) {
           float* row = rbase + (nt * 8 + r) * kRow;
 #pragma unroll
-          for (int i = 0; i < kTiles; ++i) {
-            row[2 * i] = acc[i][nt][r];
-            row[2 * i + 1] = acc[i][nt][r + 2];
-          }
+          for (int i = 0; i < kTiles; ++i)
+            *reinterpret_cast<float2*>(row + 2 * i) = make_float2(acc[i][nt][r], acc[i][nt][r + 2]);
         }
       }
   }
-  __syncthreads();
-
-  // ---- k groups -> this CTA's partial tile -> the owner CTA of each column range ----
-  // CTA q of the cluster owns columns [q WS / Ck, (q + 1) WS / Ck); every CTA writes its
-  // partial sums of those columns into the owner's receive slots (slot q), one cluster
-  // barrier makes them visible, and the owner adds the Ck slots in a fixed order.
-  const float* red = reinterpret_cast<const float*>(smem);
-  // columns per owner: ceil(WS / Ck) rounded up to even, so col / cw < Ck for every
-  // column (the last owners may get fewer columns)
-  const int cw = ((WS + p.Ck - 1) / p.Ck + 1) & ~1;
-  float* slots = reinterpret_cast<float*>(smem + p.slotoff);  // [Ck][N][cw], written by peers
-  for (int e = threadIdx.x; e < p.N * (WS / 2); e += kThreads) {
-    const int n = e / (WS / 2), col = 2 * (e - n * (WS / 2));
-    float lo = 0.0f, hi = 0.0f;
+  named_bar_sync(1, CW * 32);
+  // sum the k groups in order; Ck == 1: that is the result, else it goes to the send
+  // tile, one block of N x cwp floats per owner CTA. Thread t keeps one column pair and
+  // walks the batch rows (WS / 2 divides the consumer thread count).
+  float* send = reinterpret_cast<float*>(smem + p.sendoff);
+  {
+    constexpr int kPairs = WS / 2, kDn = CW * 32 / kPairs;
+    static_assert(CW * 32 % kPairs == 0, "column pairs per pass");
+    const int col = 2 * (threadIdx.x % kPairs);
+    const int o = col / cw, lc = col - o * cw;
+    const float* src = park + col + 2 * (col / MR);
+    for (int n = threadIdx.x / kPairs; n < p.N; n += kDn) {
+      float lo = 0.0f, hi = 0.0f;
 #pragma unroll
-    for (int g = 0; g < kKG; ++g) {
-      const float* rr = red + (g * p.N + n) * kRow + col + (col >> 5);
-      lo += rr[0];
-      hi += rr[1];
-    }
-    if (p.Ck == 1) {
-      store_half2(p.out + static_cast<size_t>(n) * p.M + c0 + col, lo, hi);
-    } else {
-      const int owner = col / cw, lc = col - owner * cw;
-      const uint32_t a = smem_u32(slots + (q * p.N + n) * cw + lc);
-      st_shared_cluster_v2(mapa_shared(a, static_cast<uint32_t>(owner)), lo, hi);
+      for (int g = 0; g < kKG; ++g) {
+        const float2 v = *reinterpret_cast<const float2*>(src + (g * p.N + n) * kRow);
+        lo += v.x;
+        hi += v.y;
+      }
+      if (p.Ck == 1)
+        store_half2(p.out + static_cast<size_t>(n) * p.M + c0 + col, lo, hi);
+      else
+        *reinterpret_cast<float2*>(send + (o * p.N + n) * cwp + lc) = make_float2(lo, hi);
     }
   }
   if (p.Ck == 1) return;
-  cluster_sync();  // every slot of this CTA is written
-  const int mine = min(cw, WS - q * cw);  // columns this CTA owns (may be <= 0)
-  for (int e = threadIdx.x; e < p.N * (mine / 2); e += kThreads) {
-    const int n = e / (mine / 2), lc = 2 * (e - n * (mine / 2));
-    float lo = 0.0f, hi = 0.0f;
-    for (int c = 0; c < p.Ck; ++c) {
-      const float2 v = *reinterpret_cast<const float2*>(slots + (c * p.N + n) * cw + lc);
-      lo += v.x;
-      hi += v.y;
+
+  // ---- partial tiles -> owner CTAs: one bulk copy per peer, completion on its rbar ----
+  fence_proxy_async_smem();
+  named_bar_sync(1, CW * 32);
+  cluster_wait();  // phase 0: every peer's rbar is initialised
+  const float* recv = reinterpret_cast<const float*>(smem + p.recvoff);  // [Ck][N][cwp], slot = sender
+  if (threadIdx.x == 0) {
+    for (int o = 0; o < p.Ck; ++o) {
+      if (o == q) continue;
+      bulk_copy_to_peer(mapa_shared(smem_u32(recv) + static_cast<uint32_t>(q) * blk, static_cast<uint32_t>(o)),
+                        send + o * p.N * cwp, blk, mapa_shared(smem_u32(rbar), static_cast<uint32_t>(o)));
     }
-    store_half2(p.out + static_cast<size_t>(n) * p.M + c0 + q * cw + lc, lo, hi);
   }
+  if (!mbar_wait(rbar, 0) && lane == 0 && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
+  const int mine = min(cw, WS - q * cw);  // columns this CTA owns (may be <= 0)
+  if (mine > 0) {
+    // thread t: column pair i, batch row n of item t of the [N][mine / 2] grid, advanced
+    // by the thread count without a division in the loop
+    const int mp = mine / 2, T = CW * 32;
+    const int dn = T / mp, di = T - dn * mp;
+    int n = threadIdx.x / mp, i = threadIdx.x - n * mp;
+    while (n < p.N) {
+      const int lc = 2 * i;
+      float lo = 0.0f, hi = 0.0f;
+      for (int c = 0; c < p.Ck; ++c) {
+        const float* src = (c == q) ? send + (q * p.N + n) * cwp : recv + (c * p.N + n) * cwp;
+        const float2 v = *reinterpret_cast<const float2*>(src + lc);
+        lo += v.x;
+        hi += v.y;
+      }
+      store_half2(p.out + static_cast<size_t>(n) * p.M + c0 + q * cw + lc, lo, hi);
+      n += dn;
+      i += di;
+      if (i >= mp) {
+        i -= mp;
+        ++n;
+      }
+    }
+  }
+  // phase 1: every block addressed to this CTA has landed (a relaxed arrival: a release
+  // would first wait for this thread's output stores, which the phase does not need)
+  cluster_arrive_relaxed();
+  cluster_wait();  // phase 1: no peer still reads this CTA's send tile
 }
 
 // ---------------------------------------------------------------------------
@@ -429,7 +529,8 @@ __global__ void __launch_bounds__(128) k_gemm_generic(const uint16_t* __restrict
 // Host side
 // ---------------------------------------------------------------------------
 struct Plan {
-  int ws = 0, P = 1, Ck = 1, nt = 1, S = 0, smem = 0, xstride = 0, xbytes = 0, ctas = 0, slotoff = 0;
+  int ws = 0, P = 1, Ck = 1, nt = 1, S = 0, smem = 0, ctas = 0;
+  int xchunks = 0, xcstride = 0, xbytes = 0, sendoff = 0, baroff = 0, recvoff = 0;
   bool fast = false;
   bool solo = false;  // one CTA per SM
 };
@@ -442,13 +543,20 @@ static int stage_bytes_of(int ws, int P) {
   return P == 1 ? Layout<128, 1>::kStageBytes : Layout<128, 2>::kStageBytes;
 }
 
-// bytes of the k-group parking tile [kKG][N][row] of the final reduction, which reuses
-// the stage ring and the activation slice
-static int reduce_bytes(int nt, int ws, int N) {
+static inline int round_up(int x, int a) { return (x + a - 1) / a * a; }
+
+// bytes of the k-group parking tile [kKG][N][kRow] of the final reduction
+static int park_bytes(int nt, int ws, int N) {
   const int mr = std::min(32 / nt, ws / 8);
   const int kg = kCW / (ws / (8 * mr));
-  const int row = (ws + ws / 32 + 12) / 16 * 16 + 4;
+  const int row = (ws + 2 * ws / mr - 4 + 15) / 16 * 16 + 4;  // ParkRow<ws, mr>
   return kg * N * row * 4;
+}
+
+// bytes of one owner block of partial sums (N rows x cwp floats), as in the kernel
+static int owner_block_bytes(int ws, int ck, int N) {
+  const int cw = ((ws + ck - 1) / ck + 1) & ~1;
+  return N * ((cw + 3) & ~3) * 4;
 }
 
 // Picks the strip width, K split (cluster size) and ring depth for a shape: the most
@@ -461,6 +569,7 @@ static Plan plan_gemm(int N, int K, int M, int sms) {
   const int P = (M % 256 == 0) ? 1 : ((M % 128 == 0) ? 2 : 0);
   if (P == 0) return pl;
   const int KS = (K + kSliceRows - 1) / kSliceRows;
+  const int xcstride = round_up(N * kXRow, 128);
   long long best_key = -1;
   for (int ws : {256, 128}) {
     if (ws == 256 && P != 1) continue;
@@ -469,8 +578,7 @@ static Plan plan_gemm(int N, int K, int M, int sms) {
       const long long ctas = static_cast<long long>(strips) * ck;
       if (ck > 1 && ctas > sms) break;
       const int slices = (KS + ck - 1) / ck;
-      const int xstride = slices * kSliceRows * 2 + 16;
-      const int xbytes = (N * xstride + 127) / 128 * 128;
+      const int xbytes = (slices * kSliceRows + kXChunk - 1) / kXChunk * xcstride;
       if (xbytes + 2 * stage_bytes_of(ws, P) + 2048 > kSmemBudget) continue;
       const long long used = std::min<long long>(ctas, sms);
       // one wave: more SMs first (quantised to 1/16 of the SMs), then wider strips
@@ -481,36 +589,39 @@ static Plan plan_gemm(int N, int K, int M, int sms) {
         best_key = key;
         pl.ws = ws;
         pl.Ck = ck;
-        pl.xstride = xstride;
         pl.xbytes = xbytes;
+        pl.xchunks = xbytes / xcstride;
         pl.ctas = static_cast<int>(ctas);
       }
     }
   }
   if (best_key < 0) return pl;
   pl.P = P;
+  pl.xcstride = xcstride;
   const int sb = stage_bytes_of(pl.ws, P);
   const int KSc = (KS + pl.Ck - 1) / pl.Ck;
   const int need = (KSc + kSPS - 1) / kSPS;  // stages that hold the CTA's whole slice
-  int S = (kSmemBudget - 2048 - pl.xbytes) / sb;
-  S = std::max(2, std::min(std::min(S, kMaxStages), need));
-  // the parking tile lives in the stage ring followed by the activation slice
-  const int rb = reduce_bytes(pl.nt, pl.ws, N);
-  while (S * sb + pl.xbytes < rb && S < kMaxStages) ++S;
-  if (S * sb + pl.xbytes < rb) pl.xbytes = (rb - S * sb + 127) / 128 * 128;
-  pl.S = S;
-  // receive slots of the cluster reduction (N x strip fp32), after the barriers
-  pl.slotoff = S * sb + pl.xbytes + 2 * kMaxStages * 8;
-  const int cw = ((pl.ws + pl.Ck - 1) / pl.Ck + 1) & ~1;  // columns per owner, as in the kernel
-  const int slotbytes = pl.Ck > 1 ? pl.Ck * N * cw * 4 : 0;
-  pl.smem = 1024 + pl.slotoff + slotbytes;
   // A CTA with a large share of the weights computes for long: one CTA per SM (at least
   // 116 KB), since two CTAs of one call on an SM take twice as long and hold back the
   // whole call. A small share is dominated by start-up latency: leave room for the next
   // call's CTA to start early (programmatic dependent launch) and prefetch.
-  pl.solo = static_cast<long long>(pl.ws) * ((KS + pl.Ck - 1) / pl.Ck) * kSliceRows >= 64 * 1024;
+  pl.solo = static_cast<long long>(pl.ws) * KSc * kSliceRows >= 64 * 1024;
+  const int blk = owner_block_bytes(pl.ws, pl.Ck, N);
+  const int recvbytes = pl.Ck > 1 ? pl.Ck * blk : 0;
+  const int budget = pl.solo ? 116 * 1024 : kSmemBudget;
+  int S = (budget - 2048 - pl.xbytes - recvbytes) / sb;
+  S = std::max(2, std::min(std::min(S, kMaxStages), need));
+  // the parking tile and the send tile live in the drained ring + activation region
+  pl.sendoff = round_up(park_bytes(pl.nt, pl.ws, N), 16);
+  const int rb = pl.sendoff + (pl.Ck > 1 ? pl.Ck * blk : 0);
+  while (S * sb + pl.xbytes < rb && S < kMaxStages) ++S;
+  pl.S = S;
+  pl.baroff = round_up(std::max(S * sb + pl.xbytes, rb), 16);
+  pl.recvoff = pl.baroff + (2 * kMaxStages + 2) * 8;  // full, empty, rbar (+ pad)
+  pl.smem = 1024 + pl.recvoff + recvbytes;
+  if (pl.smem > 113 * 1024) pl.solo = true;  // two CTAs do not fit an SM anyway: take the registers
   if (pl.solo) pl.smem = std::max(pl.smem, 116 * 1024);
-  pl.fast = true;
+  pl.fast = pl.smem <= 227 * 1024;
   return pl;
 }
 
@@ -560,9 +671,11 @@ static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, u
   prm.KS = (K + kSliceRows - 1) / kSliceRows;
   prm.Ck = pl.Ck;
   prm.S = pl.S;
-  prm.xstride = pl.xstride;
-  prm.xbytes = pl.xbytes;
-  prm.slotoff = pl.slotoff;
+  prm.xchunks = pl.xchunks;
+  prm.xcstride = pl.xcstride;
+  prm.sendoff = pl.sendoff;
+  prm.baroff = pl.baroff;
+  prm.recvoff = pl.recvoff;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((M / WS) * pl.Ck);
