@@ -32,6 +32,8 @@
 //    full 144-byte super-block rows (WS = 256), or a 16-byte scale row plus a
 //    nibble row padded to 80 / 96 bytes by the TMA box (WS = 128, M % 256 == 128).
 #include <algorithm>
+#include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 
@@ -559,61 +561,35 @@ static int owner_block_bytes(int ws, int ck, int N) {
   return N * ((cw + 3) & ~3) * 4;
 }
 
-// Picks the strip width, K split (cluster size) and ring depth for a shape: the most
-// CTAs that fit one wave of the SMs (all SMs stream the weights), then no cluster
-// (no cross-CTA reduction), then the wider strip (activations read fewer times).
-static Plan plan_gemm(int N, int K, int M, int sms) {
+// The complete launch plan of one (strip width, cluster size) candidate: ring depth,
+// shared-memory layout and residency. pl.fast is false if it does not fit.
+static Plan make_plan(int N, int KS, int P, int ws, int ck) {
   Plan pl;
   pl.nt = N <= 8 ? 1 : (N <= 16 ? 2 : 4);
-  if (K % 8 != 0 || M % 128 != 0) return pl;
-  const int P = (M % 256 == 0) ? 1 : ((M % 128 == 0) ? 2 : 0);
-  if (P == 0) return pl;
-  const int KS = (K + kSliceRows - 1) / kSliceRows;
-  const int xcstride = round_up(N * kXRow, 128);
-  long long best_key = -1;
-  for (int ws : {256, 128}) {
-    if (ws == 256 && P != 1) continue;
-    const int strips = M / ws;
-    for (int ck = 1; ck <= kMaxCk && ck <= KS; ++ck) {
-      const long long ctas = static_cast<long long>(strips) * ck;
-      if (ck > 1 && ctas > sms) break;
-      const int slices = (KS + ck - 1) / ck;
-      const int xbytes = (slices * kSliceRows + kXChunk - 1) / kXChunk * xcstride;
-      if (xbytes + 2 * stage_bytes_of(ws, P) + 2048 > kSmemBudget) continue;
-      const long long used = std::min<long long>(ctas, sms);
-      // one wave: more SMs first (quantised to 1/16 of the SMs), then wider strips
-      // (wider per-thread runs: fewer instructions per weight), then fewer CTAs per
-      // cluster
-      const long long key = (used * 16 / sms) * 1000 + ws / 64 * 10 + (8 - ck);
-      if (key > best_key) {
-        best_key = key;
-        pl.ws = ws;
-        pl.Ck = ck;
-        pl.xbytes = xbytes;
-        pl.xchunks = xbytes / xcstride;
-        pl.ctas = static_cast<int>(ctas);
-      }
-    }
-  }
-  if (best_key < 0) return pl;
   pl.P = P;
-  pl.xcstride = xcstride;
-  const int sb = stage_bytes_of(pl.ws, P);
-  const int KSc = (KS + pl.Ck - 1) / pl.Ck;
+  pl.ws = ws;
+  pl.Ck = ck;
+  pl.xcstride = round_up(N * kXRow, 128);
+  const int KSc = (KS + ck - 1) / ck;
+  pl.xbytes = (KSc * kSliceRows + kXChunk - 1) / kXChunk * pl.xcstride;
+  pl.xchunks = pl.xbytes / pl.xcstride;
+  const int sb = stage_bytes_of(ws, P);
+  if (pl.xbytes + 2 * sb + 2048 > 220 * 1024) return pl;  // a large activation slice makes the CTA solo
   const int need = (KSc + kSPS - 1) / kSPS;  // stages that hold the CTA's whole slice
   // A CTA with a large share of the weights computes for long: one CTA per SM (at least
   // 116 KB), since two CTAs of one call on an SM take twice as long and hold back the
   // whole call. A small share is dominated by start-up latency: leave room for the next
   // call's CTA to start early (programmatic dependent launch) and prefetch.
-  pl.solo = static_cast<long long>(pl.ws) * KSc * kSliceRows >= 64 * 1024;
-  const int blk = owner_block_bytes(pl.ws, pl.Ck, N);
-  const int recvbytes = pl.Ck > 1 ? pl.Ck * blk : 0;
-  const int budget = pl.solo ? 116 * 1024 : kSmemBudget;
+  pl.solo = static_cast<long long>(ws) * KSc * kSliceRows >= 64 * 1024;
+  const int blk = owner_block_bytes(ws, ck, N);
+  const int recvbytes = ck > 1 ? ck * blk : 0;
+  if (pl.xbytes + 2 * sb + 2048 > kSmemBudget) pl.solo = true;
+  const int budget = pl.solo ? std::max(116 * 1024, pl.xbytes + recvbytes + 2048 + 2 * sb) : kSmemBudget;
   int S = (budget - 2048 - pl.xbytes - recvbytes) / sb;
   S = std::max(2, std::min(std::min(S, kMaxStages), need));
   // the parking tile and the send tile live in the drained ring + activation region
-  pl.sendoff = round_up(park_bytes(pl.nt, pl.ws, N), 16);
-  const int rb = pl.sendoff + (pl.Ck > 1 ? pl.Ck * blk : 0);
+  pl.sendoff = round_up(park_bytes(pl.nt, ws, N), 16);
+  const int rb = pl.sendoff + (ck > 1 ? ck * blk : 0);
   while (S * sb + pl.xbytes < rb && S < kMaxStages) ++S;
   pl.S = S;
   pl.baroff = round_up(std::max(S * sb + pl.xbytes, rb), 16);
@@ -622,6 +598,123 @@ static Plan plan_gemm(int N, int K, int M, int sms) {
   if (pl.smem > 113 * 1024) pl.solo = true;  // two CTAs do not fit an SM anyway: take the registers
   if (pl.solo) pl.smem = std::max(pl.smem, 116 * 1024);
   pl.fast = pl.smem <= 227 * 1024;
+  return pl;
+}
+
+template <int NT, int WS, int P, int MINB>
+static int max_clusters_q(int ck, int smem) {
+  auto kern = k_gemm_int4<NT, WS, P, kCW, MINB>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ck * 16);
+  cfg.blockDim = dim3((kCW + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = ck;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -1;
+  }
+  return n;
+}
+
+// How many clusters of a plan the GPU holds at once (cudaOccupancyMaxActiveClusters on
+// the plan's own kernel). Without a device: the counts measured on B200 for one CTA per
+// SM (clusters of 7 and 8 fit only 15 times: a GPC holds two), scaled to the SM count.
+static int max_clusters(const Plan& pl, int sms) {
+  int n = -1;
+  const int minb = pl.solo ? 1 : 2;
+#define MB_Q(NT_, WS_, P_)                                                                  \
+  if (pl.nt == NT_ && pl.ws == WS_ && pl.P == P_)                                           \
+    n = minb == 1 ? max_clusters_q<NT_, WS_, P_, 1>(pl.Ck, pl.smem) : max_clusters_q<NT_, WS_, P_, 2>(pl.Ck, pl.smem);
+  MB_Q(1, 256, 1) MB_Q(1, 128, 1) MB_Q(1, 128, 2) MB_Q(2, 256, 1) MB_Q(2, 128, 1) MB_Q(2, 128, 2)
+  MB_Q(4, 256, 1) MB_Q(4, 128, 1) MB_Q(4, 128, 2)
+#undef MB_Q
+  if (n > 0) return n;
+  static const int solo148[kMaxCk + 1] = {0, 148, 74, 45, 33, 26, 22, 15, 15};
+  const int base = solo148[pl.Ck] * sms / 148;
+  return pl.solo ? base : 2 * base;
+}
+
+// Estimated time (ns) of one call under a plan, fitted to measurements on B200:
+//  * ~3.75 us of fixed cost (launch hand-off, activation copy, first weight stage,
+//    cross-CTA reduction);
+//  * the dequant loop at ~34 / 23 / 15 weights per cycle per SM for thread runs of
+//    32 / 16 / 8 columns (MR), ~1.85 GHz under load;
+//  * the weight stream at ~6.5 TB/s as a floor;
+//  * a cluster grid larger than the clusters the GPU holds at once runs in two waves.
+static double plan_cost(const Plan& pl, int N, int K, int M, int KS, int sms) {
+  const int KSc = (KS + pl.Ck - 1) / pl.Ck;
+  const double w_cta = static_cast<double>(pl.ws) * KSc * kSliceRows;
+  const int mr = std::min(32 / pl.nt, pl.ws / 8);
+  const double rate = mr >= 32 ? 34.0 : (mr >= 16 ? 23.0 : 15.0);
+  double t = 3750.0 + w_cta / rate / 1.85;
+  const double bytes = static_cast<double>(K) * M * kSB / 256 + 2.0 * N * (K + M);
+  t = std::max(t, 1500.0 + bytes / 6500.0);  // 6.5 TB/s = 6500 bytes per ns
+  if (pl.Ck > 1 && pl.ctas / pl.Ck > max_clusters(pl, sms)) t += 4000.0;
+  return t;
+}
+
+// Picks the strip width and K split (cluster size) with the lowest estimated time;
+// ties go to the wider strip and fewer CTAs per cluster.
+static Plan plan_gemm_uncached(int N, int K, int M, int sms) {
+  Plan best;
+  best.nt = N <= 8 ? 1 : (N <= 16 ? 2 : 4);
+  if (K % 8 != 0 || M % 128 != 0) return best;
+  const int P = (M % 256 == 0) ? 1 : ((M % 128 == 0) ? 2 : 0);
+  if (P == 0) return best;
+  const int KS = (K + kSliceRows - 1) / kSliceRows;
+  double best_t = 0.0;
+  for (int ws : {256, 128}) {
+    if (ws == 256 && P != 1) continue;
+    const int strips = M / ws;
+    for (int ck = 1; ck <= kMaxCk && ck <= KS; ++ck) {
+      const long long ctas = static_cast<long long>(strips) * ck;
+      if (ck > 1 && ctas > sms) break;  // a cluster grid must fit one wave
+      Plan pl = make_plan(N, KS, P, ws, ck);
+      if (!pl.fast) continue;
+      pl.ctas = static_cast<int>(ctas);
+      const double t = plan_cost(pl, N, K, M, KS, sms);
+      if (!best.fast || t < best_t - 1e-6) {
+        best = pl;
+        best_t = t;
+      }
+    }
+  }
+  return best;
+}
+
+// Plans are cached per (device, N, K, M): the capacity query is not free and a decode
+// loop repeats a handful of shapes.
+static Plan plan_gemm(int N, int K, int M, int sms) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    dev = -1;
+  }
+  const uint64_t key = (static_cast<uint64_t>(static_cast<uint32_t>(dev) & 0xFF) << 56) ^
+                       (static_cast<uint64_t>(N) << 48) ^ (static_cast<uint64_t>(static_cast<uint32_t>(K)) << 24) ^
+                       static_cast<uint64_t>(static_cast<uint32_t>(M));
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, Plan> cache;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const Plan pl = plan_gemm_uncached(N, K, M, sms);
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, pl);
   return pl;
 }
 
