@@ -7,7 +7,8 @@
  *     host before anything was launched (the reference uses -1 for a null / unloaded
  *     context and -2 for invalid arguments, antigravity_c_api.h:129-130);
  *   - the caller owns every buffer (antigravity_c_api.h:76-83, 131-143); all pointers
- *     are DEVICE pointers; nothing here allocates device memory;
+ *     are DEVICE pointers except the host buffers of mb_int4_gemm_host; nothing here
+ *     allocates device memory;
  *   - work is enqueued asynchronously on the caller's stream (`stream` is a
  *     cudaStream_t; NULL = legacy default stream). The reference is synchronous
  *     (waitUntilCompleted); callers that need the result on the host synchronise;
@@ -110,6 +111,17 @@ int32_t mb_lut_gather_f16(const int32_t* idx, int64_t n, const uint16_t* lut, in
  * ------------------------------------------------------------------------- */
 int32_t mb_int4_gemm(const uint16_t* act, const uint8_t* sb, uint16_t* out, int32_t N, int32_t K, int32_t M,
                      uint32_t* dev_err, void* stream);
+
+/* mb_int4_gemm with HOST activations and output: copies act_host (N x K fp16) into
+ * the caller's device staging buffer act_dev, runs the GEMM into out_dev (N x M) and
+ * copies it back to out_host, all enqueued on `stream` (cudaMemcpyAsync; pinned host
+ * memory makes the copies asynchronous, the caller synchronises before reading
+ * out_host). Mirrors the reference C entry point's flow, which writes the host
+ * activations into a shared buffer, dispatches the GEMM and waits
+ * (antigravity_c_api.cpp:185-220). sb is a DEVICE pointer (weights stay resident);
+ * nothing is allocated. */
+int32_t mb_int4_gemm_host(const uint16_t* act_host, const uint8_t* sb, uint16_t* out_host, int32_t N, int32_t K,
+                          int32_t M, uint16_t* act_dev, uint16_t* out_dev, uint32_t* dev_err, void* stream);
 
 /* Launch plan of the first 32-row block for a shape (introspection, no reference
  * counterpart). info must hold 8 int32: [0] fast path (1) or generic (0), [1] strip

@@ -28,6 +28,7 @@ SIGNATURES = {
     "mb_int4_dequant_q": (_c_i32, [_vp, _vp, _c_i64, _c_i32, _vp, _vp]),
     "mb_lut_gather_f16": (_c_i32, [_vp, _c_i64, _vp, _c_i64, _c_i32, _c_i64, _vp, _vp]),
     "mb_int4_gemm": (_c_i32, [_vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _vp, _vp]),
+    "mb_int4_gemm_host": (_c_i32, [_vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _vp, _vp, _vp, _vp]),
     "mb_int4_gemm_plan": (_c_i32, [_c_i32, _c_i32, _c_i32, ctypes.POINTER(_c_i32)]),
     "mb_int4_extract_columns": (_c_i32, [_vp, _c_i32, _c_i32, _c_i32, _c_i32, _vp, _vp]),
     "mb_exp_lut_lookup": (_c_i32, [_vp, _c_i32, _c_f, _vp, _c_i64, _vp, _vp]),
@@ -86,8 +87,15 @@ def require_cuda():
 
 
 def stream_of(device) -> int:
+    """Raw handle of torch's current stream on ``device`` (a torch.device or index)."""
     t = torch()
-    return t.cuda.current_stream(device).cuda_stream
+    idx = device.index if hasattr(device, "index") else device
+    if idx is None:
+        idx = t.cuda.current_device()
+    raw = getattr(t._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:  # the handle without building a Stream object
+        return raw(idx)
+    return t.cuda.current_stream(idx).cuda_stream
 
 
 _NP2TORCH = {np.dtype(np.float16): "float16", np.dtype(np.float32): "float32", np.dtype(np.int8): "int8",

@@ -718,10 +718,64 @@ static Plan plan_gemm(int N, int K, int M, int sms) {
   return pl;
 }
 
+// Tensor maps of a weight stream: 3-D view [144 bytes][super-blocks per period]
+// [periods of P rows], full-stage and 16-row boxes. Encoding costs a few microseconds
+// of host time per launch, so maps are cached per (address, K, M, strip, phases): a
+// decode loop streams the same weight tensors every step. A map depends only on these
+// values, so a cached entry stays valid for any tensor at that address and shape.
+template <int WS, int P>
+static bool weight_maps(const uint8_t* sb, int K, int M, WMaps* maps) {
+  using L = Layout<WS, P>;
+  struct Key {
+    const uint8_t* sb;
+    int K, M;
+    bool operator==(const Key& o) const { return sb == o.sb && K == o.K && M == o.M; }
+  };
+  struct Hash {
+    size_t operator()(const Key& k) const {
+      return std::hash<const void*>()(k.sb) ^ (static_cast<size_t>(k.K) * 0x9E3779B97F4A7C15ull) ^
+             (static_cast<size_t>(k.M) << 1);
+    }
+  };
+  static std::mutex mu;
+  static std::unordered_map<Key, WMaps, Hash> cache;
+  const Key key{sb, K, M};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *maps = it->second;
+      return true;
+    }
+  }
+  const uint64_t sbp = static_cast<uint64_t>(P) * M / 256;
+  const uint64_t dims[3] = {kSB, sbp, static_cast<uint64_t>(K / P)};
+  const uint64_t strides[2] = {kSB, sbp * kSB};
+  bool ok;
+  if (WS == 256) {
+    const uint32_t bf[3] = {kSB, 1, kStageRows}, bs[3] = {kSB, 1, kSliceRows};
+    ok = encode_tmap_3d_u8(&maps->full_a, sb, dims, strides, bf) &&
+         encode_tmap_3d_u8(&maps->slice_a, sb, dims, strides, bs);
+    maps->full_b = maps->full_a;
+    maps->slice_b = maps->slice_a;
+  } else {
+    const uint32_t sf[3] = {16, 1, kStageRows / P}, ss[3] = {16, 1, kSliceRows / P};
+    const uint32_t nf[3] = {L::kNibRow, 1, kStageRows / P}, ns[3] = {L::kNibRow, 1, kSliceRows / P};
+    ok = encode_tmap_3d_u8(&maps->full_a, sb, dims, strides, sf) &&
+         encode_tmap_3d_u8(&maps->slice_a, sb, dims, strides, ss) &&
+         encode_tmap_3d_u8(&maps->full_b, sb, dims, strides, nf) &&
+         encode_tmap_3d_u8(&maps->slice_b, sb, dims, strides, ns);
+  }
+  if (!ok) return false;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() >= 4096) cache.clear();
+  cache.emplace(key, *maps);
+  return true;
+}
+
 template <int NT, int WS, int P, int MINB>
 static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M,
                        uint32_t* err, cudaStream_t st) {
-  using L = Layout<WS, P>;
   auto kern = k_gemm_int4<NT, WS, P, kCW, MINB>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -734,26 +788,7 @@ static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, u
     attr_set[dev] = true;
   }
   WMaps maps;
-  // 3-D view of the stream: [144 bytes][super-blocks per period][periods of P rows]
-  const uint64_t sbp = static_cast<uint64_t>(P) * M / 256;
-  const uint64_t dims[3] = {kSB, sbp, static_cast<uint64_t>(K / P)};
-  const uint64_t strides[2] = {kSB, sbp * kSB};
-  bool ok;
-  if (WS == 256) {
-    const uint32_t bf[3] = {kSB, 1, kStageRows}, bs[3] = {kSB, 1, kSliceRows};
-    ok = encode_tmap_3d_u8(&maps.full_a, sb, dims, strides, bf) &&
-         encode_tmap_3d_u8(&maps.slice_a, sb, dims, strides, bs);
-    maps.full_b = maps.full_a;
-    maps.slice_b = maps.slice_a;
-  } else {
-    const uint32_t sf[3] = {16, 1, kStageRows / P}, ss[3] = {16, 1, kSliceRows / P};
-    const uint32_t nf[3] = {L::kNibRow, 1, kStageRows / P}, ns[3] = {L::kNibRow, 1, kSliceRows / P};
-    ok = encode_tmap_3d_u8(&maps.full_a, sb, dims, strides, sf) &&
-         encode_tmap_3d_u8(&maps.slice_a, sb, dims, strides, ss) &&
-         encode_tmap_3d_u8(&maps.full_b, sb, dims, strides, nf) &&
-         encode_tmap_3d_u8(&maps.slice_b, sb, dims, strides, ns);
-  }
-  if (!ok) return MB_ERR_LAUNCH;
+  if (!weight_maps<WS, P>(sb, K, M, &maps)) return MB_ERR_LAUNCH;
   GemmParams prm;
   prm.out = out;
   prm.act = act;
@@ -853,6 +888,25 @@ extern "C" {
 int32_t mb_int4_gemm(const uint16_t* act, const uint8_t* sb, uint16_t* out, int32_t N, int32_t K, int32_t M,
                      uint32_t* dev_err, void* stream) {
   return gemm_all(act, sb, out, N, K, M, dev_err, stream);
+}
+
+int32_t mb_int4_gemm_host(const uint16_t* act_host, const uint8_t* sb, uint16_t* out_host, int32_t N, int32_t K,
+                          int32_t M, uint16_t* act_dev, uint16_t* out_dev, uint32_t* dev_err, void* stream) {
+  if (!act_host || !sb || !out_host || !act_dev || !out_dev) return MB_ERR_NULL;
+  if (N < 1 || K < 1 || M < 1 || (static_cast<int64_t>(K) * M) % 256 != 0) return MB_ERR_ARGS;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t in_bytes = static_cast<size_t>(N) * K * 2, out_bytes = static_cast<size_t>(N) * M * 2;
+  if (cudaMemcpyAsync(act_dev, act_host, in_bytes, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return MB_ERR_LAUNCH;
+  }
+  const int32_t rc = gemm_all(act_dev, sb, out_dev, N, K, M, dev_err, stream);
+  if (rc != MB_OK) return rc;
+  if (cudaMemcpyAsync(out_host, out_dev, out_bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return MB_ERR_LAUNCH;
+  }
+  return MB_OK;
 }
 
 int32_t mb_int4_gemm_plan(int32_t N, int32_t K, int32_t M, int32_t* info) {

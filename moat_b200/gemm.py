@@ -29,15 +29,31 @@ def plan(N: int, K: int, M: int) -> dict:
     return dict(zip(keys, list(info)))
 
 
-def batched_gemm(activations, superblocks, K: int, M: int, out=None, dev_err=None):
+_staging = _lib.WorkspacePool()
+
+
+def batched_gemm(activations, superblocks, K: int, M: int, out=None, dev_err=None, sync: bool = True):
     """fp16 ``[N, K] x int4[K, M] -> fp16 [N, M]`` with fp32 accumulation.
 
-    activations: fp16 ``[N, K]`` (NumPy or torch CUDA); superblocks: uint8
-    ``[K*M/256*144]`` super-block stream on the same device (or NumPy); ``out``:
-    optional fp16 ``[N, M]`` CUDA tensor to write into; ``dev_err``: optional int32
-    CUDA tensor whose first word receives device error bits (bounded waits).
+    activations: fp16 ``[N, K]`` (NumPy, torch CUDA, or torch CPU); superblocks:
+    uint8 ``[K*M/256*144]`` super-block stream on the same device (or NumPy);
+    ``out``: optional fp16 ``[N, M]`` tensor to write into; ``dev_err``: optional
+    int32 CUDA tensor whose first word receives device error bits (bounded waits).
+
+    Host path: with CPU torch ``activations`` and a CPU torch ``out`` (pinned memory
+    for asynchronous copies) and the weights on a GPU, one C call copies the
+    activations in, runs the GEMM and copies the result back on the current stream
+    (``mb_int4_gemm_host``); with ``sync=False`` it returns without waiting and the
+    caller synchronises the stream before reading ``out``.
     """
     t = _lib.torch()
+    if type(activations) is t.Tensor and type(superblocks) is t.Tensor and superblocks.is_cuda:
+        if activations.is_cuda:
+            fast = _batched_gemm_device(t, activations, superblocks, K, M, out, dev_err)
+            if fast is not None:
+                return fast
+        elif type(out) is t.Tensor and not out.is_cuda:
+            return _batched_gemm_host(t, activations, superblocks, K, M, out, dev_err, sync)
     a, was_np = to_device(activations, t.float16)
     if a.dim() == 1:
         a = a.reshape(1, -1)
@@ -57,6 +73,63 @@ def batched_gemm(activations, superblocks, K: int, M: int, out=None, dev_err=Non
                              stream_of(a.device)), "mb_int4_gemm")
     if was_np:
         return out.cpu().numpy()
+    return out
+
+
+def _batched_gemm_device(t, a, sb, K: int, M: int, out, dev_err):
+    """The common case with few Python-side checks: contiguous fp16 CUDA activations,
+    uint8 CUDA weights on the same device. Returns None to fall back to the general
+    path for anything else."""
+    if a.dtype is not t.float16 or sb.dtype is not t.uint8 or a.device != sb.device or not a.is_contiguous():
+        return None
+    shape = a.shape
+    if len(shape) == 2:
+        N = shape[0]
+        if shape[1] != K:
+            raise ValueError(f"activations have {shape[1]} columns, expected K={K}")
+    elif len(shape) == 1 and shape[0] == K:
+        N = 1
+    else:
+        return None
+    if (K * M) % 256 != 0:
+        raise ValueError(f"K*M = {K * M} is not a multiple of 256")
+    if sb.numel() != K * M // 256 * 144:
+        raise ValueError(f"superblock stream has {sb.numel()} bytes, expected {K * M // 256 * 144}")
+    dev = a.device
+    if out is None:
+        out = t.empty((N, M), dtype=t.float16, device=dev)
+    elif out.dtype is not t.float16 or out.device != dev or out.numel() != N * M or not out.is_contiguous():
+        raise ValueError("out must be a contiguous fp16 [N, M] tensor on the activations' device")
+    rc = lib().mb_int4_gemm(a.data_ptr(), sb.data_ptr(), out.data_ptr(), N, K, M,
+                            dev_err.data_ptr() if dev_err is not None else None, stream_of(dev))
+    if rc != 0:
+        check(rc, "mb_int4_gemm")
+    return out
+
+
+def _batched_gemm_host(t, a, sb, K: int, M: int, out, dev_err, sync: bool):
+    if a.dim() == 1:
+        a = a.reshape(1, -1)
+    N = a.shape[0]
+    if a.dtype != t.float16 or not a.is_contiguous() or a.shape[1] != K:
+        raise ValueError(f"activations must be a contiguous fp16 [N, {K}] tensor")
+    if out.dtype != t.float16 or not out.is_contiguous() or tuple(out.shape) != (N, M):
+        raise ValueError(f"out must be a contiguous fp16 [{N}, {M}] tensor")
+    if (K * M) % 256 != 0:
+        raise ValueError(f"K*M = {K * M} is not a multiple of 256")
+    if sb.dtype != t.uint8 or sb.numel() != K * M // 256 * 144:
+        raise ValueError(f"superblock stream must be uint8 with {K * M // 256 * 144} bytes")
+    dev = sb.device
+    st = stream_of(dev)
+    # device staging for the activations and the output, reused by the calls of this stream
+    nin, nout = N * K * 2, N * M * 2
+    buf = _staging.get(dev, st, ((nin + 255) // 256) * 256 + nout)
+    base = buf.data_ptr()
+    check(lib().mb_int4_gemm_host(a.data_ptr(), sb.data_ptr(), out.data_ptr(), N, K, M, base,
+                                  base + ((nin + 255) // 256) * 256,
+                                  ptr(dev_err) if dev_err is not None else None, st), "mb_int4_gemm_host")
+    if sync:
+        t.cuda.current_stream(dev).synchronize()
     return out
 
 

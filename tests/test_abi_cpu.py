@@ -84,6 +84,8 @@ def test_host_side_argument_validation(L):
     fake = ctypes.c_void_p(0x10000)  # never dereferenced: validation fails first
     # null pointers -> MB_ERR_NULL (-1)
     assert L.mb_int4_gemm(None, fake, fake, 8, 2048, 2048, None, None) == -1
+    assert L.mb_int4_gemm_host(fake, fake, fake, 8, 2048, 2048, None, fake, None, None) == -1
+    assert L.mb_int4_gemm_host(fake, fake, fake, 8, 3, 5, fake, fake, None, None) == -2
     assert L.mb_int4_dequant(None, fake, 1, None) == -1
     assert L.mb_decode_attn(None, fake, fake, fake, 1, 1, 16, 128, 1.0, fake, 32768, 16.0, fake, 1 << 30, None) == -1
     # bad shapes -> MB_ERR_ARGS (-2)

@@ -127,3 +127,27 @@ def test_numpy_host_inputs_end_to_end(cuda):
     assert isinstance(y, np.ndarray) and y.dtype == np.float16 and y.shape == (N, M)
     close(y, O.gemm(x, O.unpack_superblock_weights(st).reshape(K, M)))
 
+
+
+@pytest.mark.parametrize("N", [1, 5, 32, 40])
+def test_host_buffer_path_matches_device_path(cuda, N):
+    """mb_int4_gemm_host (pinned host activations in, host output out, one C call)
+    gives the device path's bits; asynchronous calls on one stream reuse the staging
+    buffers in order."""
+    import torch
+    from moat_b200.gemm import batched_gemm
+    K, M = 512, 1024
+    st = O.quantize_pack_matrix(O.make_weights(K, M, 5))
+    sb = torch.from_numpy(st).cuda()
+    xs = [O.make_activations(N, K, 10 + i) for i in range(3)]
+    refs = [batched_gemm(torch.from_numpy(x).cuda(), sb, K, M).cpu().numpy() for x in xs]
+    hx = [torch.from_numpy(x).pin_memory() for x in xs]
+    hy = [torch.empty((N, M), dtype=torch.float16).pin_memory() for _ in xs]
+    got = batched_gemm(hx[0], sb, K, M, out=hy[0])  # synchronous
+    np.testing.assert_array_equal(got.numpy().view(np.uint16), refs[0].view(np.uint16))
+    for i in range(3):
+        batched_gemm(hx[i], sb, K, M, out=hy[i], sync=False)
+    torch.cuda.synchronize()
+    for i in range(3):
+        np.testing.assert_array_equal(hy[i].numpy().view(np.uint16), refs[i].view(np.uint16))
+    close(hy[2].numpy(), O.gemm(xs[2], O.unpack_superblock_weights(st).reshape(K, M)))
