@@ -108,26 +108,31 @@ struct AttnWs {
 };
 
 constexpr int kAttnBlock = 256;
+constexpr int kAttnU = 2;  // rows in flight per thread group in the streaming passes
 
 static inline int attn_chunks(int L) { return std::max(1, std::min(64, (L + 255) / 256)); }
 
 // Pass 1: scores for one (trace, head) and one chunk of the KV length.
-// Each group of d/8 threads handles one key row (16 bytes per thread).
+// A group of TPR = d / 8 threads owns TPR consecutive key rows per pass; each thread
+// holds an 8-value slice of d and forms its partial dot product for all TPR rows, then
+// a transposing butterfly (TPR - 1 shuffles for TPR rows) leaves thread `sub` with
+// the full dot product of row `sub`.
+template <int TPR>
 __global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __restrict__ q,
-                                                            const uint16_t* __restrict__ k, int L, int d, int C,
+                                                            const uint16_t* __restrict__ k, int L, int C,
                                                             float scale, AttnWs w) {
+  constexpr int D = TPR * 8;
+  constexpr int G = kAttnBlock / TPR;  // thread groups
+  constexpr int B = TPR < 8 ? TPR : 8;  // key rows loaded per batch
   __shared__ float sh[32];
   const int row = blockIdx.y;  // t*H + h
   const int chunk = blockIdx.x;
   const int Lc = (L + C - 1) / C;
   const int l0 = chunk * Lc, l1 = min(L, l0 + Lc);
-  const int tpr = d / 8;                 // threads per key row
-  const int rows_par = kAttnBlock / tpr; // rows in flight per iteration
-  const int sub = threadIdx.x % tpr, rgrp = threadIdx.x / tpr;
-  const bool active = rgrp < rows_par;
+  const int sub = threadIdx.x % TPR, grp = threadIdx.x / TPR;
   float qf[8];
   {
-    const uint4 qv = *reinterpret_cast<const uint4*>(q + static_cast<int64_t>(row) * d + sub * 8);
+    const uint4 qv = *reinterpret_cast<const uint4*>(q + static_cast<int64_t>(row) * D + sub * 8);
     const __half2* h = reinterpret_cast<const __half2*>(&qv);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -137,26 +142,49 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __re
     }
   }
   if (chunk == 0 && threadIdx.x == 0) w.counters[row] = 0u;  // pass 3's arrival counter
-  const uint16_t* kb = k + static_cast<int64_t>(row) * L * d;
+  const uint16_t* kb = k + static_cast<int64_t>(row) * L * D;
   float m = -INFINITY;
-  for (int base = l0; base < l1; base += rows_par) {  // uniform trip count: shuffles below
-    const int l = base + rgrp;
-    float dot = 0.0f;
-    if (active && l < l1) {
-      const uint4 kv = __ldcs(reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(l) * d + sub * 8));
-      const __half2* h = reinterpret_cast<const __half2*>(&kv);
+  for (int pbase = l0; pbase < l1; pbase += G * TPR) {  // uniform trip count: shuffles below
+    const int base = pbase + grp * TPR;
+    float v[TPR];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(h[i]);
-        dot = fmaf(qf[2 * i], f.x, dot);
-        dot = fmaf(qf[2 * i + 1], f.y, dot);
+    for (int j0 = 0; j0 < TPR; j0 += B) {
+      uint4 kv[B];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const int l = base + j0 + b;
+        kv[b] = l < l1 ? __ldcs(reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(l) * D + sub * 8))
+                       : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const __half2* h = reinterpret_cast<const __half2*>(&kv[b]);
+        float dot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h[i]);
+          dot = fmaf(qf[2 * i], f.x, dot);
+          dot = fmaf(qf[2 * i + 1], f.y, dot);
+        }
+        v[j0 + b] = dot;
       }
     }
-    for (int o = tpr / 2; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    if (active && l < l1 && sub == 0) {
-      const float s = dot * scale;
-      w.scores[static_cast<int64_t>(row) * L + l] = s;
-      m = nanmax_f(m, s);
+    // butterfly: at width s, lanes with bit s set keep rows j + s, the others rows j
+#pragma unroll
+    for (int s = TPR / 2; s >= 1; s >>= 1) {
+      const bool up = (sub & s) != 0;
+#pragma unroll
+      for (int j = 0; j < s; ++j) {
+        const float send = up ? v[j] : v[j + s];
+        const float keep = up ? v[j + s] : v[j];
+        v[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+      }
+    }
+    const int l = base + sub;
+    if (l < l1) {
+      const float sc = v[0] * scale;
+      w.scores[static_cast<int64_t>(row) * L + l] = sc;
+      m = nanmax_f(m, sc);
     }
   }
   m = block_reduce_max<kAttnBlock>(m, sh);
@@ -173,7 +201,17 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_stats(int L, int C, const u
   m = block_reduce_max<kAttnBlock>(m, sh);
   const float* s = w.scores + static_cast<int64_t>(row) * L;
   float acc = 0.0f;
-  for (int l = threadIdx.x; l < L; l += kAttnBlock) acc += lut_exp(table, __ldcg(s + l) - m, step, size);
+  for (int l0 = threadIdx.x; l0 < L; l0 += kAttnBlock * kAttnU) {  // kAttnU loads in flight, summed in order
+    float x[kAttnU];
+#pragma unroll
+    for (int u = 0; u < kAttnU; ++u) {
+      const int l = l0 + u * kAttnBlock;
+      x[u] = l < L ? __ldcg(s + l) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kAttnU; ++u)
+      if (l0 + u * kAttnBlock < L) acc += lut_exp(table, x[u] - m, step, size);
+  }
   acc = block_reduce_sum<kAttnBlock>(acc, sh);
   if (threadIdx.x == 0) {
     w.stats[2 * row] = m;
@@ -181,47 +219,66 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_stats(int L, int C, const u
   }
 }
 
-// Pass 3: out = sum_l fp16(LUT(s_l - m) / sum) * v_l, one chunk per CTA.
+// Pass 3: out = sum_l fp16(LUT(s_l - m) / sum) * v_l, one chunk per CTA. A group of
+// TPR threads owns TPR consecutive rows per pass: thread `sub` forms the probability of
+// row `sub` once, and a shuffle hands it to the group for that row's products.
+template <int TPR>
 __global__ void __launch_bounds__(kAttnBlock) k_attn_pv(const uint16_t* __restrict__ v, uint16_t* __restrict__ out,
-                                                        int L, int d, int C, const uint16_t* __restrict__ table,
+                                                        int L, int C, const uint16_t* __restrict__ table,
                                                         int size, float step, AttnWs w) {
+  constexpr int D = TPR * 8;
+  constexpr int G = kAttnBlock / TPR;
+  constexpr int B = TPR < 8 ? TPR : 8;
   __shared__ float red[kAttnBlock * 8];
   __shared__ int is_last;
   const int row = blockIdx.y, chunk = blockIdx.x;
   const int Lc = (L + C - 1) / C;
   const int l0 = chunk * Lc, l1 = min(L, l0 + Lc);
-  const int tpr = d / 8, rows_par = kAttnBlock / tpr;
-  const int sub = threadIdx.x % tpr, rgrp = threadIdx.x / tpr;
-  const bool active = rgrp < rows_par;
+  const int sub = threadIdx.x % TPR, grp = threadIdx.x / TPR;
   const float m = w.stats[2 * row], sum = w.stats[2 * row + 1];
   const float* s = w.scores + static_cast<int64_t>(row) * L;
-  const uint16_t* vb = v + static_cast<int64_t>(row) * L * d;
+  const uint16_t* vb = v + static_cast<int64_t>(row) * L * D;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-  if (active) {
-    for (int l = l0 + rgrp; l < l1; l += rows_par) {
-      const float e = lut_exp(table, __ldcg(s + l) - m, step, size);
-      const float p = __half2float(__float2half_rn(__fdiv_rn(e, sum)));
-      const uint4 vv = __ldcs(reinterpret_cast<const uint4*>(vb + static_cast<int64_t>(l) * d + sub * 8));
-      const __half2* h = reinterpret_cast<const __half2*>(&vv);
+  for (int pbase = l0; pbase < l1; pbase += G * TPR) {  // uniform trip count: shuffles below
+    const int base = pbase + grp * TPR;
+    float p = 0.0f;
+    if (base + sub < l1) {
+      const float e = lut_exp(table, __ldcg(s + base + sub) - m, step, size);
+      p = __half2float(__float2half_rn(__fdiv_rn(e, sum)));
+    }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(h[i]);
-        acc[2 * i] = fmaf(p, f.x, acc[2 * i]);
-        acc[2 * i + 1] = fmaf(p, f.y, acc[2 * i + 1]);
+    for (int j0 = 0; j0 < TPR; j0 += B) {
+      uint4 vv[B];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const int l = base + j0 + b;
+        vv[b] = l < l1 ? __ldcs(reinterpret_cast<const uint4*>(vb + static_cast<int64_t>(l) * D + sub * 8))
+                       : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const float pj = __shfl_sync(0xffffffffu, p, j0 + b, TPR);  // zero past l1
+        const __half2* h = reinterpret_cast<const __half2*>(&vv[b]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h[i]);
+          acc[2 * i] = fmaf(pj, f.x, acc[2 * i]);
+          acc[2 * i + 1] = fmaf(pj, f.y, acc[2 * i + 1]);
+        }
       }
     }
   }
-  // reduce across the row groups (fixed order): red[rgrp][d]
+  // reduce across the row groups (fixed order): red[grp][D]
 #pragma unroll
-  for (int i = 0; i < 8; ++i) red[threadIdx.x * 8 + i] = active ? acc[i] : 0.0f;  // index = (rgrp*tpr+sub)*8+i
+  for (int i = 0; i < 8; ++i) red[threadIdx.x * 8 + i] = acc[i];  // index = (grp*TPR+sub)*8+i
   __syncthreads();
-  float* part = w.part + static_cast<int64_t>(row) * C * d;
-  for (int dd = threadIdx.x; dd < d; dd += kAttnBlock) {
+  float* part = w.part + static_cast<int64_t>(row) * C * D;
+  for (int dd = threadIdx.x; dd < D; dd += kAttnBlock) {
     float t = 0.0f;
-    for (int g = 0; g < rows_par; ++g) t += red[g * d + dd];
-    __stcg(part + static_cast<int64_t>(chunk) * d + dd, t);
+    for (int g = 0; g < G; ++g) t += red[g * D + dd];
+    __stcg(part + static_cast<int64_t>(chunk) * D + dd, t);
   }
   __threadfence();
   __syncthreads();
@@ -229,10 +286,10 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_pv(const uint16_t* __restri
   __syncthreads();
   if (is_last) {  // the last chunk sums all chunks in chunk order: deterministic
     __threadfence();
-    for (int dd = threadIdx.x; dd < d; dd += kAttnBlock) {
+    for (int dd = threadIdx.x; dd < D; dd += kAttnBlock) {
       float t = 0.0f;
-      for (int c = 0; c < C; ++c) t += __ldcg(part + static_cast<int64_t>(c) * d + dd);
-      out[static_cast<int64_t>(row) * d + dd] = __half_as_ushort(__float2half_rn(t));
+      for (int c = 0; c < C; ++c) t += __ldcg(part + static_cast<int64_t>(c) * D + dd);
+      out[static_cast<int64_t>(row) * D + dd] = __half_as_ushort(__float2half_rn(t));
     }
   }
 }
@@ -264,6 +321,21 @@ static AttnWs carve_attn_ws(void* base, int T, int H, int L, int d, int C, size_
 // mb_decode_attn_workspace_size(T, H, L, d) bytes, 256-byte aligned; arguments
 // already validated by the caller. Used by the fixed-scratch entry point
 // (attention_noalloc.cu).
+template <int TPR>
+static int32_t attn_launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int L, int C,
+                           int rows, float scale, const uint16_t* table, int size, float step, const AttnWs& w,
+                           cudaStream_t st) {
+  k_attn_scores<TPR><<<dim3(C, rows), kAttnBlock, 0, st>>>(q, k, L, C, scale, w);
+  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
+  k_attn_stats<<<rows, kAttnBlock, 0, st>>>(L, C, table, size, step, w);
+  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
+  k_attn_pv<TPR><<<dim3(C, rows), kAttnBlock, 0, st>>>(v, out, L, C, table, size, step, w);
+  return launch_status();
+}
+
+// The three passes of mb_decode_attn over a scratch base that holds at least
+// mb_decode_attn_workspace_size(T, H, L, d) bytes, 256-byte aligned; arguments
+// already validated by the caller (d a power of two in [8, 256]).
 int32_t decode_attn_enqueue(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int T, int H,
                             int L, int d, float scale, const uint16_t* table, int size, float range_max,
                             void* scratch, cudaStream_t st) {
@@ -271,12 +343,15 @@ int32_t decode_attn_enqueue(const uint16_t* q, const uint16_t* k, const uint16_t
   AttnWs w = carve_attn_ws(scratch, T, H, L, d, C, nullptr);
   const float step = static_cast<float>(static_cast<double>(range_max) / (size - 1));
   const int rows = T * H;
-  k_attn_scores<<<dim3(C, rows), kAttnBlock, 0, st>>>(q, k, L, d, C, scale, w);
-  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
-  k_attn_stats<<<rows, kAttnBlock, 0, st>>>(L, C, table, size, step, w);
-  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
-  k_attn_pv<<<dim3(C, rows), kAttnBlock, 0, st>>>(v, out, L, d, C, table, size, step, w);
-  return launch_status();
+  switch (d) {
+    case 8: return attn_launch<1>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
+    case 16: return attn_launch<2>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
+    case 32: return attn_launch<4>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
+    case 64: return attn_launch<8>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
+    case 128: return attn_launch<16>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
+    case 256: return attn_launch<32>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
+    default: return MB_ERR_ARGS;
+  }
 }
 
 }  // namespace mb
@@ -324,17 +399,8 @@ int32_t mb_decode_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
   if (static_cast<int64_t>(T) * H > 65535) return MB_ERR_UNSUPPORTED;
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(workspace, 256)) return MB_ERR_ALIGN;
   if (workspace_bytes < mb_decode_attn_workspace_size(T, H, L, d)) return MB_ERR_WORKSPACE;
-  const int C = attn_chunks(L);
-  AttnWs w = carve_attn_ws(workspace, T, H, L, d, C, nullptr);
-  const float step = static_cast<float>(static_cast<double>(range_max) / (size - 1));
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int rows = T * H;
-  k_attn_scores<<<dim3(C, rows), kAttnBlock, 0, st>>>(q, k, L, d, C, scale, w);
-  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
-  k_attn_stats<<<rows, kAttnBlock, 0, st>>>(L, C, table, size, step, w);
-  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
-  k_attn_pv<<<dim3(C, rows), kAttnBlock, 0, st>>>(v, out, L, d, C, table, size, step, w);
-  return launch_status();
+  return decode_attn_enqueue(q, k, v, out, T, H, L, d, scale, table, size, range_max, workspace,
+                             static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -67,7 +67,7 @@ def test_attention_reduced_config4_golden(cuda, golden, golden_meta):
 
 
 @pytest.mark.parametrize("T,H,L,d", [(1, 1, 1, 128), (2, 3, 77, 64), (1, 2, 4097, 128), (3, 1, 300, 256),
-                                     (2, 2, 1000, 8)])
+                                     (2, 2, 1000, 8), (1, 3, 20000, 16), (2, 1, 513, 32)])
 def test_attention_ragged(cuda, T, H, L, d):
     from moat_b200.attention import ExponentialLUT, decode_attention
     q, k, v = OA.make_attention_inputs(T, H, L, d, L + d)
