@@ -342,6 +342,8 @@ def run_moat(args):
         if all(str(n) in per for n in sweep) and world == 1:
             tr = sum(per[str(n)] for n in sweep) / len(sweep)
 
+    attn = None if (world > 1 or args.no_attn) else attention_side(dev, peak, peak_kind)
+
     if rank == 0:
         cpu = None if (world > 1 or args.no_cpu) else cpu_reference(budget_s=args.cpu_seconds)
         line = {
@@ -365,12 +367,62 @@ def run_moat(args):
             "clocks": clk,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "attention": attn,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         graphs.clear()
         dist.destroy_process_group()
     return 0
+
+
+def attention_side(dev, peak, peak_kind, reps: int = 10):
+    """BASELINE config 4 decode attention (16 traces x 16 heads, KV length 4096, d 128,
+    fp16 KV, 32,768-entry LUT over [-16, 0]) timed on its own with CUDA events: two KV
+    copies alternate so each call streams from HBM (2 x 537 MB > L2). Reported beside
+    the GEMM line, not part of its value."""
+    import torch
+    from moat_b200 import _lib
+    from moat_b200.attention import ExponentialLUT, attention_bytes
+    L = _lib.lib()
+    T, H, Lk, d = 16, 16, 4096, 128
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 7)
+    q = torch.randn((T, H, d), generator=g, device=dev).half()
+    kv = [(torch.randn((T, H, Lk, d), generator=g, device=dev).half(),
+           torch.randn((T, H, Lk, d), generator=g, device=dev).half()) for _ in range(2)]
+    lut = ExponentialLUT(range_max=16.0)
+    tab = lut.device_table(dev)
+    out = torch.empty((T, H, d), dtype=torch.float16, device=dev)
+    nb = int(L.mb_decode_attn_workspace_size(T, H, Lk, d))
+    ws = torch.zeros(nb, dtype=torch.uint8, device=dev)
+    st = torch.cuda.Stream(device=dev)
+    scale = 1.0 / float(d) ** 0.5
+
+    def call(i):
+        k, v = kv[i % 2]
+        rc = L.mb_decode_attn(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), T, H, Lk, d, scale,
+                              tab.data_ptr(), lut.size, 16.0, ws.data_ptr(), nb, st.cuda_stream)
+        assert rc == 0, rc
+
+    with torch.cuda.stream(st):
+        for i in range(4):
+            call(i)
+        st.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for i in range(reps):
+            call(i)
+        e1.record(st)
+        st.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    b = attention_bytes(T, H, Lk, d)
+    gbs = b / us / 1e3
+    del kv, ws
+    return {"workload": "BASELINE config 4: LUT-softmax decode attention, 16 traces x 16 heads, L=4096, d=128",
+            "us_per_call": us, "GBps": gbs, "bytes_per_call": b, "kernels_per_call": 3,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "peak_kind": peak_kind}}
 
 
 def run_e2e(args, dev, stream, shard, sweep, Ms, world, rank, bounds, R):
@@ -437,6 +489,7 @@ def main():
     ap.add_argument("--sweep", default=",".join(map(str, SWEEP)))
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-attn", action="store_true", help="skip the config-4 attention side measurement")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--e2e-ring", type=int, default=36)
     ap.add_argument("--e2e-steps", type=int, default=3)

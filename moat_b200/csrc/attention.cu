@@ -108,9 +108,9 @@ struct AttnWs {
 };
 
 constexpr int kAttnBlock = 256;
-constexpr int kAttnU = 2;  // rows in flight per thread group in the streaming passes
+constexpr int kAttnU = 8;  // score loads in flight per thread in the statistics pass
 
-static inline int attn_chunks(int L) { return std::max(1, std::min(64, (L + 255) / 256)); }
+static inline int attn_chunks(int L) { return std::max(1, std::min(64, (L + 511) / 512)); }
 
 // Pass 1: scores for one (trace, head) and one chunk of the KV length.
 // A group of TPR = d / 8 threads owns TPR consecutive key rows per pass; each thread
@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __re
                                                             float scale, AttnWs w) {
   constexpr int D = TPR * 8;
   constexpr int G = kAttnBlock / TPR;  // thread groups
-  constexpr int B = TPR < 8 ? TPR : 8;  // key rows loaded per batch
+  constexpr int B = TPR;  // key rows loaded per batch: a group's rows all in flight
   __shared__ float sh[32];
   const int row = blockIdx.y;  // t*H + h
   const int chunk = blockIdx.x;
