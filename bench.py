@@ -342,7 +342,7 @@ def run_moat(args):
         if all(str(n) in per for n in sweep) and world == 1:
             tr = sum(per[str(n)] for n in sweep) / len(sweep)
 
-    attn = None if (world > 1 or args.no_attn) else attention_side(dev, peak, peak_kind)
+    attn = None if (world > 1 or args.no_attn) else attention_side(dev, peak, peak_kind, with_cpu=not args.no_cpu)
 
     if rank == 0:
         cpu = None if (world > 1 or args.no_cpu) else cpu_reference(budget_s=args.cpu_seconds)
@@ -376,7 +376,7 @@ def run_moat(args):
     return 0
 
 
-def attention_side(dev, peak, peak_kind, reps: int = 10):
+def attention_side(dev, peak, peak_kind, reps: int = 10, with_cpu: bool = True):
     """BASELINE config 4 decode attention (16 traces x 16 heads, KV length 4096, d 128,
     fp16 KV, 32,768-entry LUT over [-16, 0]) timed on its own with CUDA events: two KV
     copies alternate so each call streams from HBM (2 x 537 MB > L2). Reported beside
@@ -422,7 +422,29 @@ def attention_side(dev, peak, peak_kind, reps: int = 10):
     return {"workload": "BASELINE config 4: LUT-softmax decode attention, 16 traces x 16 heads, L=4096, d=128",
             "us_per_call": us, "GBps": gbs, "bytes_per_call": b, "kernels_per_call": 3,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                         "peak_kind": peak_kind}}
+                         "peak_kind": peak_kind},
+            "cpu_baseline": attention_cpu_baseline(T, H, Lk, d) if with_cpu else None}
+
+
+def attention_cpu_baseline(T, H, Lk, d, budget_s: float = 6.0):
+    """The reference's CPU composition of decode attention (NumPy einsum scores, LUT
+    softmax, einsum with V; oracle port) on the host cores, one full config-4 call per
+    sample until the budget is spent."""
+    from oracle import attention as OA
+    from moat_b200.attention import attention_bytes
+    q, k, v = OA.make_attention_inputs(T, H, Lk, d, SEED + 11)
+    tbl = OA.exp_table(32768, 16.0)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        OA.decode_attention(q, k, v, tbl, 16.0)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or calls >= 20:
+            break
+    return {"value": attention_bytes(T, H, Lk, d) * calls / el / 1e9, "unit": "GB/s", "cores": os.cpu_count(),
+            "kind": "port", "sample": f"{calls} full config-4 calls ({el:.1f} s) of the NumPy composition "
+                                       "(einsum scores, LUT softmax, einsum with V)",
+            "us_per_call": el / calls * 1e6}
 
 
 def run_e2e(args, dev, stream, shard, sweep, Ms, world, rank, bounds, R):
