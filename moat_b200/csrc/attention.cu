@@ -130,6 +130,10 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __re
   const int Lc = (L + C - 1) / C;
   const int l0 = chunk * Lc, l1 = min(L, l0 + Lc);
   const int sub = threadIdx.x % TPR, grp = threadIdx.x / TPR;
+  // q and K may come from the previous kernel, and the workspace is still read by the
+  // previous call's last pass: wait for it, then let the next pass launch
+  pdl_wait();
+  pdl_launch_dependents();
   float qf[8];
   {
     const uint4 qv = *reinterpret_cast<const uint4*>(q + static_cast<int64_t>(row) * D + sub * 8);
@@ -196,6 +200,8 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_stats(int L, int C, const u
                                                            float step, AttnWs w) {
   __shared__ float sh[32];
   const int row = blockIdx.x;
+  pdl_wait();  // the scores pass has finished
+  pdl_launch_dependents();
   float m = -INFINITY;
   for (int c = threadIdx.x; c < C; c += kAttnBlock) m = nanmax_f(m, w.cmax[static_cast<int64_t>(row) * C + c]);
   m = block_reduce_max<kAttnBlock>(m, sh);
@@ -235,9 +241,19 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_pv(const uint16_t* __restri
   const int Lc = (L + C - 1) / C;
   const int l0 = chunk * Lc, l1 = min(L, l0 + Lc);
   const int sub = threadIdx.x % TPR, grp = threadIdx.x / TPR;
+  const uint16_t* vb = v + static_cast<int64_t>(row) * L * D;
+  // Every kernel of this path lets its successor launch only after its own wait, so
+  // when this one starts, the kernel before the scores pass (the producer of V) has
+  // finished: V of the first pass can be pulled into L2 while the statistics pass runs.
+  for (int l = l0 + threadIdx.x / (D / 64 > 0 ? D / 64 : 1); l < min(l1, l0 + G * TPR);
+       l += kAttnBlock / (D / 64 > 0 ? D / 64 : 1)) {
+    const int part = D >= 64 ? threadIdx.x % (D / 64) : 0;  // 128-byte lines of a row
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(vb + static_cast<int64_t>(l) * D + part * 64));
+  }
+  pdl_wait();  // the statistics pass has finished
+  pdl_launch_dependents();
   const float m = w.stats[2 * row], sum = w.stats[2 * row + 1];
   const float* s = w.scores + static_cast<int64_t>(row) * L;
-  const uint16_t* vb = v + static_cast<int64_t>(row) * L * D;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
@@ -321,16 +337,37 @@ static AttnWs carve_attn_ws(void* base, int T, int H, int L, int d, int C, size_
 // mb_decode_attn_workspace_size(T, H, L, d) bytes, 256-byte aligned; arguments
 // already validated by the caller. Used by the fixed-scratch entry point
 // (attention_noalloc.cu).
+// Launch with programmatic dependent launch: the kernel may start while its
+// predecessor on the stream finishes; it waits (griddepcontrol.wait) before touching
+// anything the predecessor writes.
+template <typename Kern, typename... Args>
+static int launch_pdl(Kern kern, dim3 grid, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kAttnBlock);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, args...) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return MB_ERR_LAUNCH;
+  }
+  return MB_OK;
+}
+
 template <int TPR>
 static int32_t attn_launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int L, int C,
                            int rows, float scale, const uint16_t* table, int size, float step, const AttnWs& w,
                            cudaStream_t st) {
-  k_attn_scores<TPR><<<dim3(C, rows), kAttnBlock, 0, st>>>(q, k, L, C, scale, w);
-  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
-  k_attn_stats<<<rows, kAttnBlock, 0, st>>>(L, C, table, size, step, w);
-  if (launch_status() != MB_OK) return MB_ERR_LAUNCH;
-  k_attn_pv<TPR><<<dim3(C, rows), kAttnBlock, 0, st>>>(v, out, L, C, table, size, step, w);
-  return launch_status();
+  if (launch_pdl(k_attn_scores<TPR>, dim3(C, rows), st, q, k, L, C, scale, w) != MB_OK) return MB_ERR_LAUNCH;
+  if (launch_pdl(k_attn_stats, dim3(rows), st, L, C, table, size, step, w) != MB_OK) return MB_ERR_LAUNCH;
+  if (launch_pdl(k_attn_pv<TPR>, dim3(C, rows), st, v, out, L, C, table, size, step, w) != MB_OK)
+    return MB_ERR_LAUNCH;
+  return MB_OK;
 }
 
 // The three passes of mb_decode_attn over a scratch base that holds at least
