@@ -43,6 +43,7 @@ extern "C" {
 
 /* Device-side error word bits (written to a caller-provided device word). */
 #define MB_DEVERR_TIMEOUT 1u /* a bounded wait gave up */
+#define MB_DEVERR_INDEX 2u   /* a device-side index (token id, position) was out of range */
 
 #define MB_ABI_VERSION 1
 
@@ -180,6 +181,55 @@ int32_t mb_decode_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
 int32_t mb_decode_attn_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int32_t T,
                                int32_t H, int32_t L, int32_t d, float scale, const uint16_t* table, int32_t size,
                                float range_max, void* stream);
+
+/* Decode attention over a KV cache with room for Lmax positions per (trace, head):
+ * k_cache / v_cache [T, H, Lmax, d], the first L positions valid; otherwise exactly
+ * mb_decode_attn (same workspace size for (T, H, L, d)). The decode step's attention
+ * over its growing cache (reference: Attention.forward with kv_cache,
+ * transformer.py:80-121, LUT softmax as in batch_generator.py:226,234). */
+int32_t mb_decode_attn_cache(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, uint16_t* out,
+                             int32_t T, int32_t H, int32_t L, int32_t Lmax, int32_t d, float scale,
+                             const uint16_t* table, int32_t size, float range_max, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decoder-step glue (the element-wise and row-wise operations between the INT4
+ * GEMMs of one decode step; reference: antigravity-engine/src/transformer.py).
+ * The residual stream x is fp32 [N, D]; GEMM inputs and outputs are fp16.
+ * ------------------------------------------------------------------------- */
+/* x[n] = fp32(table[ids[n]]) for fp16 table [V, D] (TinyLlamaModel embed_tokens,
+ * transformer.py:184, 207). An id outside [0, V) gives a zero row and sets
+ * MB_DEVERR_INDEX in the optional device word dev_err. */
+int32_t mb_embed(const int32_t* ids, int32_t N, const uint16_t* table, int32_t V, int32_t D, float* x,
+                 uint32_t* dev_err, void* stream);
+
+/* x += y (y may be NULL), then h = fp16(x * rsqrt(mean(x^2) + eps) * w): the residual
+ * add fused with RMSNorm (transformer.py:26-37, 148-158); w fp32 [D]. */
+int32_t mb_add_rmsnorm(float* x, const uint16_t* y, const float* w, int32_t N, int32_t D, float eps, uint16_t* h,
+                       void* stream);
+
+/* RoPE on the q and k parts of qkv [N, 3*H*dh] (q | k | v, heads contiguous) at the
+ * per-trace positions pos[N] (device), adjacent pairs rotated as in
+ * apply_rotary_emb (transformer.py:39-63); cs = fp32 (cos, sin) pairs [Lmax][dh/2].
+ * Writes q_out [N, H, dh] and appends k and v at pos into k_cache / v_cache
+ * [N, H, Lmax, dh]. A position outside [0, Lmax) skips the row and sets
+ * MB_DEVERR_INDEX. */
+int32_t mb_rope_append(const uint16_t* qkv, int32_t N, int32_t H, int32_t dh, const int32_t* pos, const float* cs,
+                       int32_t Lmax, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, uint32_t* dev_err,
+                       void* stream);
+
+/* a[n, j] = fp16(silu(gu[n, j]) * gu[n, F + j]) for gu [N, 2F] (gate | up), the SwiGLU
+ * of SwiGLUMLP.forward (transformer.py:124-134). */
+int32_t mb_swiglu(const uint16_t* gu, int32_t N, int32_t F, uint16_t* a, void* stream);
+
+/* ids[n] = first index of the largest value of logits[n, :] (fp16 [N, V]); a NaN
+ * counts as the largest, like numpy.argmax (greedy sampling, batch_generator.py:203-206,
+ * 224-227). */
+int32_t mb_argmax_f16(const uint16_t* logits, int32_t N, int32_t V, int32_t* ids, void* stream);
+
+/* pos[n] += 1 on the device (the next decode step's positions; no reference
+ * counterpart: keeps a captured step replayable). */
+int32_t mb_advance_positions(int32_t* pos, int32_t N, void* stream);
 
 #ifdef __cplusplus
 }

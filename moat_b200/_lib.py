@@ -36,6 +36,14 @@ SIGNATURES = {
     "mb_decode_attn_workspace_size": (_c_sz, [_c_i32, _c_i32, _c_i32, _c_i32]),
     "mb_decode_attn": (_c_i32, [_vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _c_f, _vp, _c_i32, _c_f,
                                 _vp, _c_sz, _vp]),
+    "mb_decode_attn_cache": (_c_i32, [_vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_f, _vp,
+                                      _c_i32, _c_f, _vp, _c_sz, _vp]),
+    "mb_embed": (_c_i32, [_vp, _c_i32, _vp, _c_i32, _c_i32, _vp, _vp, _vp]),
+    "mb_add_rmsnorm": (_c_i32, [_vp, _vp, _vp, _c_i32, _c_i32, _c_f, _vp, _vp]),
+    "mb_rope_append": (_c_i32, [_vp, _c_i32, _c_i32, _c_i32, _vp, _vp, _c_i32, _vp, _vp, _vp, _vp, _vp]),
+    "mb_swiglu": (_c_i32, [_vp, _c_i32, _c_i32, _vp, _vp]),
+    "mb_argmax_f16": (_c_i32, [_vp, _c_i32, _c_i32, _vp, _vp]),
+    "mb_advance_positions": (_c_i32, [_vp, _c_i32, _vp]),
     "mb_decode_attn_noalloc": (_c_i32, [_vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _c_f, _vp, _c_i32,
                                         _c_f, _vp]),
 }

@@ -119,8 +119,8 @@ static inline int attn_chunks(int L) { return std::max(1, std::min(64, (L + 511)
 // the full dot product of row `sub`.
 template <int TPR>
 __global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __restrict__ q,
-                                                            const uint16_t* __restrict__ k, int L, int C,
-                                                            float scale, AttnWs w) {
+                                                            const uint16_t* __restrict__ k, int L, int64_t kvs,
+                                                            int C, float scale, AttnWs w) {
   constexpr int D = TPR * 8;
   constexpr int G = kAttnBlock / TPR;  // thread groups
   constexpr int B = TPR;  // key rows loaded per batch: a group's rows all in flight
@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __re
     }
   }
   if (chunk == 0 && threadIdx.x == 0) w.counters[row] = 0u;  // pass 3's arrival counter
-  const uint16_t* kb = k + static_cast<int64_t>(row) * L * D;
+  const uint16_t* kb = k + static_cast<int64_t>(row) * kvs;
   float m = -INFINITY;
   for (int pbase = l0; pbase < l1; pbase += G * TPR) {  // uniform trip count: shuffles below
     const int base = pbase + grp * TPR;
@@ -230,7 +230,7 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_stats(int L, int C, const u
 // row `sub` once, and a shuffle hands it to the group for that row's products.
 template <int TPR>
 __global__ void __launch_bounds__(kAttnBlock) k_attn_pv(const uint16_t* __restrict__ v, uint16_t* __restrict__ out,
-                                                        int L, int C, const uint16_t* __restrict__ table,
+                                                        int L, int64_t kvs, int C, const uint16_t* __restrict__ table,
                                                         int size, float step, AttnWs w) {
   constexpr int D = TPR * 8;
   constexpr int G = kAttnBlock / TPR;
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_pv(const uint16_t* __restri
   const int Lc = (L + C - 1) / C;
   const int l0 = chunk * Lc, l1 = min(L, l0 + Lc);
   const int sub = threadIdx.x % TPR, grp = threadIdx.x / TPR;
-  const uint16_t* vb = v + static_cast<int64_t>(row) * L * D;
+  const uint16_t* vb = v + static_cast<int64_t>(row) * kvs;
   // Every kernel of this path lets its successor launch only after its own wait, so
   // when this one starts, the kernel before the scores pass (the producer of V) has
   // finished: V of the first pass can be pulled into L2 while the statistics pass runs.
@@ -360,33 +360,35 @@ static int launch_pdl(Kern kern, dim3 grid, cudaStream_t st, Args... args) {
 }
 
 template <int TPR>
-static int32_t attn_launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int L, int C,
-                           int rows, float scale, const uint16_t* table, int size, float step, const AttnWs& w,
+static int32_t attn_launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int L, int64_t kvs,
+                           int C, int rows, float scale, const uint16_t* table, int size, float step, const AttnWs& w,
                            cudaStream_t st) {
-  if (launch_pdl(k_attn_scores<TPR>, dim3(C, rows), st, q, k, L, C, scale, w) != MB_OK) return MB_ERR_LAUNCH;
+  if (launch_pdl(k_attn_scores<TPR>, dim3(C, rows), st, q, k, L, kvs, C, scale, w) != MB_OK) return MB_ERR_LAUNCH;
   if (launch_pdl(k_attn_stats, dim3(rows), st, L, C, table, size, step, w) != MB_OK) return MB_ERR_LAUNCH;
-  if (launch_pdl(k_attn_pv<TPR>, dim3(C, rows), st, v, out, L, C, table, size, step, w) != MB_OK)
+  if (launch_pdl(k_attn_pv<TPR>, dim3(C, rows), st, v, out, L, kvs, C, table, size, step, w) != MB_OK)
     return MB_ERR_LAUNCH;
   return MB_OK;
 }
 
 // The three passes of mb_decode_attn over a scratch base that holds at least
 // mb_decode_attn_workspace_size(T, H, L, d) bytes, 256-byte aligned; arguments
-// already validated by the caller (d a power of two in [8, 256]).
+// already validated by the caller (d a power of two in [8, 256]). kv_stride: elements
+// between the K (and V) rows of consecutive (trace, head) pairs; 0 = L * d (packed).
 int32_t decode_attn_enqueue(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int T, int H,
                             int L, int d, float scale, const uint16_t* table, int size, float range_max,
-                            void* scratch, cudaStream_t st) {
+                            void* scratch, cudaStream_t st, int64_t kv_stride) {
   const int C = attn_chunks(L);
   AttnWs w = carve_attn_ws(scratch, T, H, L, d, C, nullptr);
   const float step = static_cast<float>(static_cast<double>(range_max) / (size - 1));
   const int rows = T * H;
+  const int64_t kvs = kv_stride > 0 ? kv_stride : static_cast<int64_t>(L) * d;
   switch (d) {
-    case 8: return attn_launch<1>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
-    case 16: return attn_launch<2>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
-    case 32: return attn_launch<4>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
-    case 64: return attn_launch<8>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
-    case 128: return attn_launch<16>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
-    case 256: return attn_launch<32>(q, k, v, out, L, C, rows, scale, table, size, step, w, st);
+    case 8: return attn_launch<1>(q, k, v, out, L, kvs, C, rows, scale, table, size, step, w, st);
+    case 16: return attn_launch<2>(q, k, v, out, L, kvs, C, rows, scale, table, size, step, w, st);
+    case 32: return attn_launch<4>(q, k, v, out, L, kvs, C, rows, scale, table, size, step, w, st);
+    case 64: return attn_launch<8>(q, k, v, out, L, kvs, C, rows, scale, table, size, step, w, st);
+    case 128: return attn_launch<16>(q, k, v, out, L, kvs, C, rows, scale, table, size, step, w, st);
+    case 256: return attn_launch<32>(q, k, v, out, L, kvs, C, rows, scale, table, size, step, w, st);
     default: return MB_ERR_ARGS;
   }
 }
@@ -437,7 +439,23 @@ int32_t mb_decode_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(workspace, 256)) return MB_ERR_ALIGN;
   if (workspace_bytes < mb_decode_attn_workspace_size(T, H, L, d)) return MB_ERR_WORKSPACE;
   return decode_attn_enqueue(q, k, v, out, T, H, L, d, scale, table, size, range_max, workspace,
-                             static_cast<cudaStream_t>(stream));
+                             static_cast<cudaStream_t>(stream), 0);
+}
+
+int32_t mb_decode_attn_cache(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, uint16_t* out,
+                             int32_t T, int32_t H, int32_t L, int32_t Lmax, int32_t d, float scale,
+                             const uint16_t* table, int32_t size, float range_max, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (!q || !k_cache || !v_cache || !out || !table || !workspace) return MB_ERR_NULL;
+  if (T < 1 || H < 1 || L < 1 || Lmax < L || d < 8 || d > 256 || (d & (d - 1)) != 0 || size < 2 ||
+      !(range_max > 0.0f))
+    return MB_ERR_ARGS;
+  if (static_cast<int64_t>(T) * H > 65535) return MB_ERR_UNSUPPORTED;
+  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(workspace, 256))
+    return MB_ERR_ALIGN;
+  if (workspace_bytes < mb_decode_attn_workspace_size(T, H, L, d)) return MB_ERR_WORKSPACE;
+  return decode_attn_enqueue(q, k_cache, v_cache, out, T, H, L, d, scale, table, size, range_max, workspace,
+                             static_cast<cudaStream_t>(stream), static_cast<int64_t>(Lmax) * d);
 }
 
 }  // extern "C"

@@ -85,6 +85,13 @@ def test_host_side_argument_validation(L):
     # null pointers -> MB_ERR_NULL (-1)
     assert L.mb_int4_gemm(None, fake, fake, 8, 2048, 2048, None, None) == -1
     assert L.mb_int4_gemm_host(fake, fake, fake, 8, 2048, 2048, None, fake, None, None) == -1
+    assert L.mb_embed(None, 4, fake, 10, 16, fake, None, None) == -1
+    assert L.mb_add_rmsnorm(fake, None, fake, 0, 16, 1e-6, fake, None) == -2
+    assert L.mb_rope_append(fake, 2, 2, 7, fake, fake, 16, fake, fake, fake, None, None) == -2   # odd head dim
+    assert L.mb_swiglu(fake, 2, 0, fake, None) == -2
+    assert L.mb_argmax_f16(None, 2, 10, fake, None) == -1
+    assert L.mb_decode_attn_cache(fake, fake, fake, fake, 1, 1, 20, 10, 128, 1.0, fake, 32768, 16.0, fake,
+                                  1 << 30, None) == -2  # L > Lmax
     assert L.mb_int4_gemm_host(fake, fake, fake, 8, 3, 5, fake, fake, None, None) == -2
     assert L.mb_int4_dequant(None, fake, 1, None) == -1
     assert L.mb_decode_attn(None, fake, fake, fake, 1, 1, 16, 128, 1.0, fake, 32768, 16.0, fake, 1 << 30, None) == -1
