@@ -192,6 +192,17 @@ int32_t mb_decode_attn_cache(const uint16_t* q, const uint16_t* k_cache, const u
                              const uint16_t* table, int32_t size, float range_max, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* mb_decode_attn_cache with the valid length read on the device: trace t uses the
+ * first min(Lmax, lens[t] + len_add) positions (lens is a DEVICE int32[T], e.g. the
+ * decode positions with len_add = 1), so one captured decode step replays while the
+ * cache grows. The grid and the workspace are sized for Lmax
+ * (mb_decode_attn_workspace_size(T, H, Lmax, d)). No reference counterpart (the
+ * reference passes the length on the host). */
+int32_t mb_decode_attn_cache_lens(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, uint16_t* out,
+                                  int32_t T, int32_t H, int32_t Lmax, int32_t d, const int32_t* lens, int32_t len_add,
+                                  float scale, const uint16_t* table, int32_t size, float range_max, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Decoder-step glue (the element-wise and row-wise operations between the INT4
  * GEMMs of one decode step; reference: antigravity-engine/src/transformer.py).

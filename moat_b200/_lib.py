@@ -38,6 +38,8 @@ SIGNATURES = {
                                 _vp, _c_sz, _vp]),
     "mb_decode_attn_cache": (_c_i32, [_vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_f, _vp,
                                       _c_i32, _c_f, _vp, _c_sz, _vp]),
+    "mb_decode_attn_cache_lens": (_c_i32, [_vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _vp, _c_i32, _c_f,
+                                           _vp, _c_i32, _c_f, _vp, _c_sz, _vp]),
     "mb_embed": (_c_i32, [_vp, _c_i32, _vp, _c_i32, _c_i32, _vp, _vp, _vp]),
     "mb_add_rmsnorm": (_c_i32, [_vp, _vp, _vp, _c_i32, _c_i32, _c_f, _vp, _vp]),
     "mb_rope_append": (_c_i32, [_vp, _c_i32, _c_i32, _c_i32, _vp, _vp, _c_i32, _vp, _vp, _vp, _vp, _vp]),

@@ -103,9 +103,19 @@ struct AttnWs {
   uint32_t* counters;  // [T*H]
   float* stats;        // [T*H][2]: row max, LUT sum
   float* cmax;         // [T*H][C]
-  float* scores;       // [T*H][L]
+  float* scores;       // [T*H][Lg]
   float* part;         // [T*H][C][d] fp32 per-chunk partial outputs
+  // Optional per-trace lengths read on the device (a captured decode step replays with
+  // a growing cache): L = min(Lg, lens[t] + len_add) for the rows of trace t = row / heads.
+  const int32_t* lens;
+  int len_add, heads;
 };
+
+// Valid key length of a (trace, head) row; Lg sizes the grid and the workspace.
+__device__ __forceinline__ int attn_len(const AttnWs& w, int row, int Lg) {
+  if (!w.lens) return Lg;
+  return max(0, min(Lg, w.lens[row / w.heads] + w.len_add));
+}
 
 constexpr int kAttnBlock = 256;
 constexpr int kAttnU = 8;  // score loads in flight per thread in the statistics pass
@@ -119,7 +129,7 @@ static inline int attn_chunks(int L) { return std::max(1, std::min(64, (L + 511)
 // the full dot product of row `sub`.
 template <int TPR>
 __global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __restrict__ q,
-                                                            const uint16_t* __restrict__ k, int L, int64_t kvs,
+                                                            const uint16_t* __restrict__ k, int Lg, int64_t kvs,
                                                             int C, float scale, AttnWs w) {
   constexpr int D = TPR * 8;
   constexpr int G = kAttnBlock / TPR;  // thread groups
@@ -127,13 +137,14 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __re
   __shared__ float sh[32];
   const int row = blockIdx.y;  // t*H + h
   const int chunk = blockIdx.x;
-  const int Lc = (L + C - 1) / C;
-  const int l0 = chunk * Lc, l1 = min(L, l0 + Lc);
+  const int Lc = (Lg + C - 1) / C;
   const int sub = threadIdx.x % TPR, grp = threadIdx.x / TPR;
   // q and K may come from the previous kernel, and the workspace is still read by the
   // previous call's last pass: wait for it, then let the next pass launch
   pdl_wait();
   pdl_launch_dependents();
+  const int L = attn_len(w, row, Lg);
+  const int l0 = chunk * Lc, l1 = min(L, l0 + Lc);
   float qf[8];
   {
     const uint4 qv = *reinterpret_cast<const uint4*>(q + static_cast<int64_t>(row) * D + sub * 8);
@@ -187,7 +198,7 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __re
     const int l = base + sub;
     if (l < l1) {
       const float sc = v[0] * scale;
-      w.scores[static_cast<int64_t>(row) * L + l] = sc;
+      w.scores[static_cast<int64_t>(row) * Lg + l] = sc;
       m = nanmax_f(m, sc);
     }
   }
@@ -196,16 +207,17 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_scores(const uint16_t* __re
 }
 
 // Pass 2: row max over the chunk maxima, fp32 sum of the LUT values.
-__global__ void __launch_bounds__(kAttnBlock) k_attn_stats(int L, int C, const uint16_t* __restrict__ table, int size,
+__global__ void __launch_bounds__(kAttnBlock) k_attn_stats(int Lg, int C, const uint16_t* __restrict__ table, int size,
                                                            float step, AttnWs w) {
   __shared__ float sh[32];
   const int row = blockIdx.x;
   pdl_wait();  // the scores pass has finished
   pdl_launch_dependents();
+  const int L = attn_len(w, row, Lg);
   float m = -INFINITY;
   for (int c = threadIdx.x; c < C; c += kAttnBlock) m = nanmax_f(m, w.cmax[static_cast<int64_t>(row) * C + c]);
   m = block_reduce_max<kAttnBlock>(m, sh);
-  const float* s = w.scores + static_cast<int64_t>(row) * L;
+  const float* s = w.scores + static_cast<int64_t>(row) * Lg;
   float acc = 0.0f;
   for (int l0 = threadIdx.x; l0 < L; l0 += kAttnBlock * kAttnU) {  // kAttnU loads in flight, summed in order
     float x[kAttnU];
@@ -230,7 +242,7 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_stats(int L, int C, const u
 // row `sub` once, and a shuffle hands it to the group for that row's products.
 template <int TPR>
 __global__ void __launch_bounds__(kAttnBlock) k_attn_pv(const uint16_t* __restrict__ v, uint16_t* __restrict__ out,
-                                                        int L, int64_t kvs, int C, const uint16_t* __restrict__ table,
+                                                        int Lg, int64_t kvs, int C, const uint16_t* __restrict__ table,
                                                         int size, float step, AttnWs w) {
   constexpr int D = TPR * 8;
   constexpr int G = kAttnBlock / TPR;
@@ -238,7 +250,9 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_pv(const uint16_t* __restri
   __shared__ float red[kAttnBlock * 8];
   __shared__ int is_last;
   const int row = blockIdx.y, chunk = blockIdx.x;
-  const int Lc = (L + C - 1) / C;
+  const int Lc = (Lg + C - 1) / C;
+  // the lengths array is not written by the passes of this call: readable before the wait
+  const int L = attn_len(w, row, Lg);
   const int l0 = chunk * Lc, l1 = min(L, l0 + Lc);
   const int sub = threadIdx.x % TPR, grp = threadIdx.x / TPR;
   const uint16_t* vb = v + static_cast<int64_t>(row) * kvs;
@@ -253,7 +267,7 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_pv(const uint16_t* __restri
   pdl_wait();  // the statistics pass has finished
   pdl_launch_dependents();
   const float m = w.stats[2 * row], sum = w.stats[2 * row + 1];
-  const float* s = w.scores + static_cast<int64_t>(row) * L;
+  const float* s = w.scores + static_cast<int64_t>(row) * Lg;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
@@ -329,6 +343,9 @@ static AttnWs carve_attn_ws(void* base, int T, int H, int L, int d, int C, size_
   off += align256(rows * C * d * 4);
   w.scores = reinterpret_cast<float*>(p + off);
   off += align256(rows * static_cast<size_t>(L) * 4);
+  w.lens = nullptr;
+  w.len_add = 0;
+  w.heads = H;
   if (total) *total = off;
   return w;
 }
@@ -374,11 +391,16 @@ static int32_t attn_launch(const uint16_t* q, const uint16_t* k, const uint16_t*
 // mb_decode_attn_workspace_size(T, H, L, d) bytes, 256-byte aligned; arguments
 // already validated by the caller (d a power of two in [8, 256]). kv_stride: elements
 // between the K (and V) rows of consecutive (trace, head) pairs; 0 = L * d (packed).
+// lens (optional, device): per-trace lengths, the valid length of trace t being
+// min(L, lens[t] + len_add); L then sizes the grid and the workspace.
 int32_t decode_attn_enqueue(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int T, int H,
                             int L, int d, float scale, const uint16_t* table, int size, float range_max,
-                            void* scratch, cudaStream_t st, int64_t kv_stride) {
+                            void* scratch, cudaStream_t st, int64_t kv_stride, const int32_t* lens,
+                            int len_add) {
   const int C = attn_chunks(L);
   AttnWs w = carve_attn_ws(scratch, T, H, L, d, C, nullptr);
+  w.lens = lens;
+  w.len_add = len_add;
   const float step = static_cast<float>(static_cast<double>(range_max) / (size - 1));
   const int rows = T * H;
   const int64_t kvs = kv_stride > 0 ? kv_stride : static_cast<int64_t>(L) * d;
@@ -439,7 +461,7 @@ int32_t mb_decode_attn(const uint16_t* q, const uint16_t* k, const uint16_t* v, 
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(workspace, 256)) return MB_ERR_ALIGN;
   if (workspace_bytes < mb_decode_attn_workspace_size(T, H, L, d)) return MB_ERR_WORKSPACE;
   return decode_attn_enqueue(q, k, v, out, T, H, L, d, scale, table, size, range_max, workspace,
-                             static_cast<cudaStream_t>(stream), 0);
+                             static_cast<cudaStream_t>(stream), 0, nullptr, 0);
 }
 
 int32_t mb_decode_attn_cache(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, uint16_t* out,
@@ -455,7 +477,22 @@ int32_t mb_decode_attn_cache(const uint16_t* q, const uint16_t* k_cache, const u
     return MB_ERR_ALIGN;
   if (workspace_bytes < mb_decode_attn_workspace_size(T, H, L, d)) return MB_ERR_WORKSPACE;
   return decode_attn_enqueue(q, k_cache, v_cache, out, T, H, L, d, scale, table, size, range_max, workspace,
-                             static_cast<cudaStream_t>(stream), static_cast<int64_t>(Lmax) * d);
+                             static_cast<cudaStream_t>(stream), static_cast<int64_t>(Lmax) * d, nullptr, 0);
+}
+
+int32_t mb_decode_attn_cache_lens(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, uint16_t* out,
+                                  int32_t T, int32_t H, int32_t Lmax, int32_t d, const int32_t* lens, int32_t len_add,
+                                  float scale, const uint16_t* table, int32_t size, float range_max, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (!q || !k_cache || !v_cache || !out || !table || !workspace || !lens) return MB_ERR_NULL;
+  if (T < 1 || H < 1 || Lmax < 1 || d < 8 || d > 256 || (d & (d - 1)) != 0 || size < 2 || !(range_max > 0.0f))
+    return MB_ERR_ARGS;
+  if (static_cast<int64_t>(T) * H > 65535) return MB_ERR_UNSUPPORTED;
+  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(workspace, 256))
+    return MB_ERR_ALIGN;
+  if (workspace_bytes < mb_decode_attn_workspace_size(T, H, Lmax, d)) return MB_ERR_WORKSPACE;
+  return decode_attn_enqueue(q, k_cache, v_cache, out, T, H, Lmax, d, scale, table, size, range_max, workspace,
+                             static_cast<cudaStream_t>(stream), static_cast<int64_t>(Lmax) * d, lens, len_add);
 }
 
 }  // extern "C"

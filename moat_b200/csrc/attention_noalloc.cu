@@ -34,7 +34,8 @@ namespace mb {
 
 int32_t decode_attn_enqueue(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int T, int H,
                             int L, int d, float scale, const uint16_t* table, int size, float range_max,
-                            void* scratch, cudaStream_t st, int64_t kv_stride);
+                            void* scratch, cudaStream_t st, int64_t kv_stride, const int32_t* lens,
+                            int len_add);
 
 constexpr size_t kNoAllocScratchBytes = static_cast<size_t>(16) << 20;
 static_assert(kNoAllocScratchBytes == MB_ATTN_NOALLOC_SCRATCH_BYTES, "header and module disagree on the limit");
@@ -88,5 +89,5 @@ extern "C" int32_t mb_decode_attn_noalloc(const uint16_t* q, const uint16_t* k, 
   const int32_t rc = noalloc_scratch(dev, &base);
   if (rc != MB_OK) return rc;
   return decode_attn_enqueue(q, k, v, out, T, H, L, d, scale, table, size, range_max, base,
-                             static_cast<cudaStream_t>(stream), 0);
+                             static_cast<cudaStream_t>(stream), 0, nullptr, 0);
 }

@@ -110,6 +110,7 @@ class Int4Decoder:
         self.pos = t.zeros((N,), dtype=t.int32, device=self.dev)
         self.err = t.zeros((1,), dtype=t.int32, device=self.dev)
         self.length = 0  # positions filled so far (the same for every trace)
+        self.graph = None
         nb = int(lib().mb_decode_attn_workspace_size(N, H, L, dh))
         self.ws = t.zeros(nb, dtype=t.uint8, device=self.dev)
         self.scale = float(np.float32(1.0 / np.sqrt(dh)))
@@ -133,9 +134,38 @@ class Int4Decoder:
     def step(self, ids):
         """One decode step for all traces: token ids [N] (int32, device) in, the greedy
         next ids [N] out (a device tensor, also kept in ``self.ids``)."""
-        cfg, N, L = self.cfg, self.N, lib()
-        if self.length >= cfg.max_len:
+        if self.length >= self.cfg.max_len:
             raise ValueError("KV cache is full")
+        self._enqueue(ids, device_lengths=False)
+        self.length += 1
+        return self.ids
+
+    def capture(self):
+        """Capture one decode step (reading ``self.ids``, writing the next ids back into
+        it) as a CUDA graph; the attention reads its length from the device positions,
+        so the graph replays unchanged while the cache grows. Run one eager step first
+        (plans and tensor maps are cached on the first call of each shape)."""
+        t = _lib.torch()
+        g = t.cuda.CUDAGraph()
+        side = t.cuda.Stream(device=self.dev)
+        side.wait_stream(t.cuda.current_stream(self.dev))
+        with t.cuda.stream(side):
+            with t.cuda.graph(g, stream=side):
+                self._enqueue(self.ids, device_lengths=True)
+        t.cuda.current_stream(self.dev).wait_stream(side)
+        self.graph = g
+        return g
+
+    def step_graphed(self):
+        """Replay the captured step: consumes ``self.ids``, leaves the next ids there."""
+        if self.length >= self.cfg.max_len:
+            raise ValueError("KV cache is full")
+        self.graph.replay()
+        self.length += 1
+        return self.ids
+
+    def _enqueue(self, ids, device_lengths: bool):
+        cfg, N, L = self.cfg, self.N, lib()
         D, H, dh, F, V = cfg.hidden, cfg.heads, cfg.head_dim, cfg.ffn, cfg.vocab
         st = stream_of(self.dev)
         p = lambda x: x.data_ptr()  # noqa: E731
@@ -147,10 +177,16 @@ class Int4Decoder:
             check(L.mb_int4_gemm(p(self.h), p(lw["wqkv"]), p(self.qkv), N, D, 3 * D, err, st), "qkv")
             check(L.mb_rope_append(p(self.qkv), N, H, dh, p(self.pos), p(self.cs), cfg.max_len, p(self.q),
                                    p(self.k_cache[li]), p(self.v_cache[li]), err, st), "mb_rope_append")
-            check(L.mb_decode_attn_cache(p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.att), N, H,
-                                         self.length + 1, cfg.max_len, dh, self.scale, p(self.table), self.lut.size,
-                                         float(self.lut.range_max), p(self.ws), self.ws.numel(), st),
-                  "mb_decode_attn_cache")
+            if device_lengths:  # length = position + 1, read on the device
+                check(L.mb_decode_attn_cache_lens(p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.att),
+                                                  N, H, cfg.max_len, dh, p(self.pos), 1, self.scale, p(self.table),
+                                                  self.lut.size, float(self.lut.range_max), p(self.ws),
+                                                  self.ws.numel(), st), "mb_decode_attn_cache_lens")
+            else:
+                check(L.mb_decode_attn_cache(p(self.q), p(self.k_cache[li]), p(self.v_cache[li]), p(self.att), N, H,
+                                             self.length + 1, cfg.max_len, dh, self.scale, p(self.table),
+                                             self.lut.size, float(self.lut.range_max), p(self.ws), self.ws.numel(),
+                                             st), "mb_decode_attn_cache")
             check(L.mb_int4_gemm(p(self.att), p(lw["wo"]), p(self.o), N, D, D, err, st), "o_proj")
             check(L.mb_add_rmsnorm(p(self.x), p(self.o), p(lw["ffn_norm"]), N, D, cfg.eps, p(self.h), st),
                   "mb_add_rmsnorm")
@@ -162,8 +198,6 @@ class Int4Decoder:
         check(L.mb_int4_gemm(p(self.h), p(self.lm_head), p(self.logits), N, D, V, err, st), "lm_head")
         check(L.mb_argmax_f16(p(self.logits), N, V, p(self.ids), st), "mb_argmax_f16")
         check(L.mb_advance_positions(p(self.pos), N, st), "mb_advance_positions")
-        self.length += 1
-        return self.ids
 
     def generate(self, first_ids, steps: int):
         """Greedy decode ``steps`` tokens from ``first_ids`` [N]; returns [steps, N] ids

@@ -204,3 +204,30 @@ def test_decoder_steps_match_fp32_reference(cuda):
         assert int(dec.err.item()) == 0
         ids = nxt.clone()
     assert dec.pos.cpu().tolist() == [13] * N
+
+
+def test_captured_step_matches_eager_steps(cuda):
+    """The CUDA-graph step (attention length read on the device) gives the eager
+    step's tokens and, within the attention's summation-order noise, its logits."""
+    import torch
+    from moat_b200.decode import DecoderConfig, Int4Decoder
+    cfg = DecoderConfig(layers=2, hidden=256, heads=2, head_dim=128, ffn=512, vocab=1000, max_len=300)
+    N = 3
+    a = Int4Decoder(cfg, N, device=cuda, seed=9)
+    b = Int4Decoder(cfg, N, device=cuda, seed=9)
+    for dec in (a, b):
+        dec.fill_prompt_cache(257, seed=2)
+    ids = torch.tensor([5, 6, 7], dtype=torch.int32, device=cuda)
+    b.ids.copy_(ids)
+    b.step(b.ids)            # one eager step caches plans and tensor maps
+    a.step(ids)
+    b.capture()
+    for _ in range(4):
+        ea = a.step(a.ids.clone()).clone()
+        eb = b.step_graphed().clone()
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(b.logits.float().cpu().numpy(), a.logits.float().cpu().numpy(),
+                                   rtol=1e-2, atol=1e-2)
+        assert eb.cpu().tolist() == ea.cpu().tolist()
+    assert a.pos.cpu().tolist() == b.pos.cpu().tolist() == [262] * N
+    assert int(b.err.item()) == 0
