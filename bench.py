@@ -343,6 +343,7 @@ def run_moat(args):
             tr = sum(per[str(n)] for n in sweep) / len(sweep)
 
     attn = None if (world > 1 or args.no_attn) else attention_side(dev, peak, peak_kind, with_cpu=not args.no_cpu)
+    decode = None if (world > 1 or args.no_decode) else decode_side(dev)
 
     if rank == 0:
         cpu = None if (world > 1 or args.no_cpu) else cpu_reference(budget_s=args.cpu_seconds)
@@ -368,6 +369,7 @@ def run_moat(args):
             "e2e": e2e,
             "cpu_baseline": cpu,
             "attention": attn,
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -447,6 +449,45 @@ def attention_cpu_baseline(T, H, Lk, d, budget_s: float = 6.0):
             "us_per_call": el / calls * 1e6}
 
 
+def decode_side(dev, steps: int = 64):
+    """BASELINE config 5 decode speed: a random-init Qwen-1.5B-like INT4 decoder (24
+    layers, hidden 2048, 16 heads x 128, FFN 5504, vocab 151936), N = 16 traces, the
+    KV cache seeded for a 512-token prompt, greedy steps replayed from one captured
+    CUDA graph and timed with CUDA events. Reported beside the GEMM line."""
+    import torch
+    from moat_b200.decode import DecoderConfig, Int4Decoder
+    cfg = DecoderConfig()
+    N, P = 16, 512
+    dec = Int4Decoder(cfg, N, device=dev, seed=SEED + 5)
+    dec.fill_prompt_cache(P, seed=SEED + 6)
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 7)
+    dec.ids.copy_(torch.randint(0, cfg.vocab, (N,), generator=g, device=dev, dtype=torch.int32))
+    dec.step(dec.ids)  # eager step: plans and tensor maps cached for the capture
+    dec.capture()
+    for _ in range(3):
+        dec.step_graphed()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        dec.step_graphed()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    err = int(dec.err.item())
+    wbytes = sum(sum(int(lw[k].numel()) for k in ("wqkv", "wo", "wgu", "wd")) for lw in dec.layers) \
+        + int(dec.lm_head.numel())
+    kv = 2 * cfg.layers * N * cfg.heads * cfg.head_dim * 2 * (P + 5 + steps // 2)  # mean cache length
+    del dec
+    torch.cuda.empty_cache()
+    return {"workload": "BASELINE config 5: 24-layer INT4 decoder, hidden 2048, 16x128 heads, FFN 5504, "
+                        "vocab 151936; 16 traces, 512-position cache, greedy", "metric": "decode tok/s",
+            "tok_per_s": N / ms * 1e3, "ms_per_step": ms, "steps": steps, "graph": True,
+            "bytes_per_step": wbytes + kv, "GBps": (wbytes + kv) / ms / 1e6, "device_error_bits": err,
+            "data": "synthetic (random-init weights quantized to INT4; KV cache seeded N(0,1))"}
+
+
 def run_e2e(args, dev, stream, shard, sweep, Ms, world, rank, bounds, R):
     """Same sweep through ``moat_b200.gemm.batched_gemm``: per call an H2D of the
     activations from pinned memory and a D2H of the output into pinned memory."""
@@ -512,6 +553,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-attn", action="store_true", help="skip the config-4 attention side measurement")
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-5 decode side measurement")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--e2e-ring", type=int, default=36)
     ap.add_argument("--e2e-steps", type=int, default=3)
