@@ -324,6 +324,133 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_pv(const uint16_t* __restri
   }
 }
 
+// All three passes in one CTA per (trace, head) row, for caches short enough that a
+// row's scores fit in shared memory (at most kAttnFusedMax positions): the scores pass
+// of k_attn_scores into shared memory, the row max and LUT sum of k_attn_stats, and
+// the P·V pass of k_attn_pv over the whole row, with the same per-element arithmetic.
+// One launch and no cross-CTA merge; the split passes keep long caches, whose rows
+// need many CTAs each to fill the GPU.
+constexpr int kAttnFusedMax = 2048;
+
+template <int TPR>
+__global__ void __launch_bounds__(kAttnBlock) k_attn_fused(const uint16_t* __restrict__ q,
+                                                           const uint16_t* __restrict__ k,
+                                                           const uint16_t* __restrict__ v, uint16_t* __restrict__ out,
+                                                           int Lg, int64_t kvs, float scale,
+                                                           const uint16_t* __restrict__ table, int size, float step,
+                                                           AttnWs w) {
+  constexpr int D = TPR * 8;
+  constexpr int G = kAttnBlock / TPR;
+  __shared__ float sh[32];
+  __shared__ float red[kAttnBlock * 8];
+  extern __shared__ float sc[];  // [Lg] scores of this row
+  const int row = blockIdx.x;
+  const int sub = threadIdx.x % TPR, grp = threadIdx.x / TPR;
+  pdl_wait();  // q, K and V may come from the previous kernel
+  pdl_launch_dependents();
+  const int L = attn_len(w, row, Lg);
+  float qf[8];
+  {
+    const uint4 qv = *reinterpret_cast<const uint4*>(q + static_cast<int64_t>(row) * D + sub * 8);
+    const __half2* h = reinterpret_cast<const __half2*>(&qv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      qf[2 * i] = f.x;
+      qf[2 * i + 1] = f.y;
+    }
+  }
+  const uint16_t* kb = k + static_cast<int64_t>(row) * kvs;
+  const uint16_t* vb = v + static_cast<int64_t>(row) * kvs;
+  // scores: a group owns TPR consecutive rows per pass (butterfly as in k_attn_scores)
+  float m = -INFINITY;
+  for (int pbase = 0; pbase < L; pbase += G * TPR) {
+    const int base = pbase + grp * TPR;
+    float vv[TPR];
+    {
+      uint4 kv[TPR];
+#pragma unroll
+      for (int b = 0; b < TPR; ++b) {
+        const int l = base + b;
+        kv[b] = l < L ? __ldcs(reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(l) * D + sub * 8))
+                      : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int b = 0; b < TPR; ++b) {
+        const __half2* h = reinterpret_cast<const __half2*>(&kv[b]);
+        float dot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h[i]);
+          dot = fmaf(qf[2 * i], f.x, dot);
+          dot = fmaf(qf[2 * i + 1], f.y, dot);
+        }
+        vv[b] = dot;
+      }
+    }
+#pragma unroll
+    for (int s = TPR / 2; s >= 1; s >>= 1) {
+      const bool up = (sub & s) != 0;
+#pragma unroll
+      for (int j = 0; j < s; ++j) {
+        const float send = up ? vv[j] : vv[j + s];
+        const float keep = up ? vv[j + s] : vv[j];
+        vv[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+      }
+    }
+    const int l = base + sub;
+    if (l < L) {
+      const float x = vv[0] * scale;
+      sc[l] = x;
+      m = nanmax_f(m, x);
+    }
+  }
+  m = block_reduce_max<kAttnBlock>(m, sh);  // synchronises: all scores are in sc[]
+  // LUT sum in the order of k_attn_stats (per thread l = t, t + block, ..., then the block)
+  float acc = 0.0f;
+  for (int l = threadIdx.x; l < L; l += kAttnBlock) acc += lut_exp(table, sc[l] - m, step, size);
+  acc = block_reduce_sum<kAttnBlock>(acc, sh);
+  const float sum = acc > 0.0f ? acc : 1.0f;
+  // P·V over the whole row
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+  for (int pbase = 0; pbase < L; pbase += G * TPR) {
+    const int base = pbase + grp * TPR;
+    float p = 0.0f;
+    if (base + sub < L) {
+      const float e = lut_exp(table, sc[base + sub] - m, step, size);
+      p = __half2float(__float2half_rn(__fdiv_rn(e, sum)));
+    }
+    uint4 vr[TPR];
+#pragma unroll
+    for (int b = 0; b < TPR; ++b) {
+      const int l = base + b;
+      vr[b] = l < L ? __ldcs(reinterpret_cast<const uint4*>(vb + static_cast<int64_t>(l) * D + sub * 8))
+                    : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int b = 0; b < TPR; ++b) {
+      const float pj = __shfl_sync(0xffffffffu, p, b, TPR);  // zero past L
+      const __half2* h = reinterpret_cast<const __half2*>(&vr[b]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        o[2 * i] = fmaf(pj, f.x, o[2 * i]);
+        o[2 * i + 1] = fmaf(pj, f.y, o[2 * i + 1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[threadIdx.x * 8 + i] = o[i];  // index = (grp*TPR+sub)*8+i
+  __syncthreads();
+  for (int dd = threadIdx.x; dd < D; dd += kAttnBlock) {
+    float t = 0.0f;
+    for (int g = 0; g < G; ++g) t += red[g * D + dd];
+    out[static_cast<int64_t>(row) * D + dd] = __half_as_ushort(__float2half_rn(t));
+  }
+}
+
 static inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 static AttnWs carve_attn_ws(void* base, int T, int H, int L, int d, int C, size_t* total) {
@@ -358,11 +485,11 @@ static AttnWs carve_attn_ws(void* base, int T, int H, int L, int d, int C, size_
 // predecessor on the stream finishes; it waits (griddepcontrol.wait) before touching
 // anything the predecessor writes.
 template <typename Kern, typename... Args>
-static int launch_pdl(Kern kern, dim3 grid, cudaStream_t st, Args... args) {
+static int launch_pdl_smem(Kern kern, dim3 grid, cudaStream_t st, size_t smem, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kAttnBlock);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -376,10 +503,23 @@ static int launch_pdl(Kern kern, dim3 grid, cudaStream_t st, Args... args) {
   return MB_OK;
 }
 
+template <typename Kern, typename... Args>
+static int launch_pdl(Kern kern, dim3 grid, cudaStream_t st, Args... args) {
+  return launch_pdl_smem(kern, grid, st, 0, args...);
+}
+
 template <int TPR>
 static int32_t attn_launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int L, int64_t kvs,
                            int C, int rows, float scale, const uint16_t* table, int size, float step, const AttnWs& w,
                            cudaStream_t st) {
+  if (L <= kAttnFusedMax) {  // one CTA per row, scores in shared memory
+    const int smem = L * 4;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(k_attn_fused<TPR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return MB_ERR_LAUNCH;
+    return launch_pdl_smem(k_attn_fused<TPR>, dim3(rows), st, static_cast<size_t>(smem), q, k, v, out, L, kvs,
+                           scale, table, size, step, w);
+  }
   if (launch_pdl(k_attn_scores<TPR>, dim3(C, rows), st, q, k, L, kvs, C, scale, w) != MB_OK) return MB_ERR_LAUNCH;
   if (launch_pdl(k_attn_stats, dim3(rows), st, L, C, table, size, step, w) != MB_OK) return MB_ERR_LAUNCH;
   if (launch_pdl(k_attn_pv<TPR>, dim3(C, rows), st, v, out, L, kvs, C, table, size, step, w) != MB_OK)

@@ -26,6 +26,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 // x[n, :] = float(table[ids[n], :])
 __global__ void __launch_bounds__(kRowBlock) k_embed(const int32_t* __restrict__ ids, const uint16_t* __restrict__ table,
                                                      int D, int V, float* __restrict__ x, uint32_t* err) {
+  pdl_wait();  // the ids may come from the previous step's argmax
+  pdl_launch_dependents();
   const int n = blockIdx.x;
   const int id = ids[n];
   if (id < 0 || id >= V) {  // out-of-range token: zero row, error bit
@@ -43,6 +45,8 @@ __global__ void __launch_bounds__(kRowBlock) k_add_rmsnorm(float* __restrict__ x
                                                            const float* __restrict__ w, int D, float eps,
                                                            uint16_t* __restrict__ h) {
   __shared__ float part[kRowBlock / 32];
+  pdl_wait();
+  pdl_launch_dependents();
   const int n = blockIdx.x;
   float* xr = x + static_cast<int64_t>(n) * D;
   float ss = 0.0f;
@@ -73,6 +77,8 @@ __global__ void __launch_bounds__(64) k_rope_append(const uint16_t* __restrict__
                                                     const int32_t* __restrict__ pos, const float2* __restrict__ cs,
                                                     int Lmax, uint16_t* __restrict__ q_out, uint16_t* __restrict__ kc,
                                                     uint16_t* __restrict__ vc, uint32_t* err) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int n = blockIdx.x / H, hh = blockIdx.x % H;
   const int p = pos[n];
   const int HD = H * dh;
@@ -98,6 +104,8 @@ __global__ void __launch_bounds__(64) k_rope_append(const uint16_t* __restrict__
 // a[n, j] = fp16(silu(g) * u) with g = gu[n, j], u = gu[n, F + j] (fp32 math).
 __global__ void __launch_bounds__(kRowBlock) k_swiglu(const uint16_t* __restrict__ gu, int F, int64_t total,
                                                       uint16_t* __restrict__ a) {
+  pdl_wait();
+  pdl_launch_dependents();
   for (int64_t e = blockIdx.x * static_cast<int64_t>(kRowBlock) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * kRowBlock) {
     const int64_t n = e / F;
@@ -115,6 +123,8 @@ __global__ void __launch_bounds__(kRowBlock) k_argmax(const uint16_t* __restrict
                                                       int32_t* __restrict__ ids) {
   __shared__ float bv[kRowBlock];
   __shared__ int bi[kRowBlock];
+  pdl_wait();
+  pdl_launch_dependents();
   const int n = blockIdx.x;
   const uint16_t* row = logits + static_cast<int64_t>(n) * V;
   float best = -INFINITY;
@@ -153,6 +163,8 @@ __global__ void __launch_bounds__(kRowBlock) k_argmax(const uint16_t* __restrict
 
 // pos[n] += 1 (the next step's position), on the device so a captured step can replay.
 __global__ void k_advance(int32_t* pos, int N) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n < N) pos[n] += 1;
 }
@@ -167,16 +179,16 @@ int32_t mb_embed(const int32_t* ids, int32_t N, const uint16_t* table, int32_t V
                  uint32_t* dev_err, void* stream) {
   if (!ids || !table || !x) return MB_ERR_NULL;
   if (N < 1 || V < 1 || D < 1) return MB_ERR_ARGS;
-  k_embed<<<N, kRowBlock, 0, static_cast<cudaStream_t>(stream)>>>(ids, table, D, V, x, dev_err);
-  return launch_status();
+  return launch_with_pdl(k_embed, dim3(N), dim3(kRowBlock), 0, static_cast<cudaStream_t>(stream), ids, table, D, V, x,
+                         dev_err);
 }
 
 int32_t mb_add_rmsnorm(float* x, const uint16_t* y, const float* w, int32_t N, int32_t D, float eps, uint16_t* h,
                        void* stream) {
   if (!x || !w || !h) return MB_ERR_NULL;
   if (N < 1 || D < 1 || !(eps >= 0.0f)) return MB_ERR_ARGS;
-  k_add_rmsnorm<<<N, kRowBlock, 0, static_cast<cudaStream_t>(stream)>>>(x, y, w, D, eps, h);
-  return launch_status();
+  return launch_with_pdl(k_add_rmsnorm, dim3(N), dim3(kRowBlock), 0, static_cast<cudaStream_t>(stream), x, y, w, D,
+                         eps, h);
 }
 
 int32_t mb_rope_append(const uint16_t* qkv, int32_t N, int32_t H, int32_t dh, const int32_t* pos, const float* cs,
@@ -186,9 +198,8 @@ int32_t mb_rope_append(const uint16_t* qkv, int32_t N, int32_t H, int32_t dh, co
   if (N < 1 || H < 1 || dh < 2 || dh % 2 != 0 || Lmax < 1) return MB_ERR_ARGS;
   if (!aligned(qkv, 4) || !aligned(q_out, 4) || !aligned(k_cache, 4) || !aligned(v_cache, 4) || !aligned(cs, 8))
     return MB_ERR_ALIGN;
-  k_rope_append<<<N * H, 64, 0, static_cast<cudaStream_t>(stream)>>>(
-      qkv, H, dh, pos, reinterpret_cast<const float2*>(cs), Lmax, q_out, k_cache, v_cache, dev_err);
-  return launch_status();
+  return launch_with_pdl(k_rope_append, dim3(N * H), dim3(64), 0, static_cast<cudaStream_t>(stream), qkv, H, dh, pos,
+                         reinterpret_cast<const float2*>(cs), Lmax, q_out, k_cache, v_cache, dev_err);
 }
 
 int32_t mb_swiglu(const uint16_t* gu, int32_t N, int32_t F, uint16_t* a, void* stream) {
@@ -196,22 +207,20 @@ int32_t mb_swiglu(const uint16_t* gu, int32_t N, int32_t F, uint16_t* a, void* s
   if (N < 1 || F < 1) return MB_ERR_ARGS;
   const int64_t total = static_cast<int64_t>(N) * F;
   const int64_t blocks = std::min<int64_t>((total + kRowBlock - 1) / kRowBlock, static_cast<int64_t>(sm_count()) * 8);
-  k_swiglu<<<static_cast<int>(blocks), kRowBlock, 0, static_cast<cudaStream_t>(stream)>>>(gu, F, total, a);
-  return launch_status();
+  return launch_with_pdl(k_swiglu, dim3(static_cast<unsigned>(blocks)), dim3(kRowBlock), 0,
+                         static_cast<cudaStream_t>(stream), gu, F, total, a);
 }
 
 int32_t mb_argmax_f16(const uint16_t* logits, int32_t N, int32_t V, int32_t* ids, void* stream) {
   if (!logits || !ids) return MB_ERR_NULL;
   if (N < 1 || V < 1) return MB_ERR_ARGS;
-  k_argmax<<<N, kRowBlock, 0, static_cast<cudaStream_t>(stream)>>>(logits, V, ids);
-  return launch_status();
+  return launch_with_pdl(k_argmax, dim3(N), dim3(kRowBlock), 0, static_cast<cudaStream_t>(stream), logits, V, ids);
 }
 
 int32_t mb_advance_positions(int32_t* pos, int32_t N, void* stream) {
   if (!pos) return MB_ERR_NULL;
   if (N < 1) return MB_ERR_ARGS;
-  k_advance<<<(N + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(pos, N);
-  return launch_status();
+  return launch_with_pdl(k_advance, dim3((N + 127) / 128), dim3(128), 0, static_cast<cudaStream_t>(stream), pos, N);
 }
 
 }  // extern "C"
