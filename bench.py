@@ -343,7 +343,7 @@ def run_moat(args):
             tr = sum(per[str(n)] for n in sweep) / len(sweep)
 
     attn = None if (world > 1 or args.no_attn) else attention_side(dev, peak, peak_kind, with_cpu=not args.no_cpu)
-    decode = None if (world > 1 or args.no_decode) else decode_side(dev)
+    decode = None if args.no_decode else decode_side(dev, rank, world)
 
     if rank == 0:
         cpu = None if (world > 1 or args.no_cpu) else cpu_reference(budget_s=args.cpu_seconds)
@@ -449,42 +449,46 @@ def attention_cpu_baseline(T, H, Lk, d, budget_s: float = 6.0):
             "us_per_call": el / calls * 1e6}
 
 
-def decode_side(dev, steps: int = 64):
+def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 64):
     """BASELINE config 5 decode speed: a random-init Qwen-1.5B-like INT4 decoder (24
     layers, hidden 2048, 16 heads x 128, FFN 5504, vocab 151936), N = 16 traces, the
     KV cache seeded for a 512-token prompt, greedy steps replayed from one captured
-    CUDA graph and timed with CUDA events. Reported beside the GEMM line."""
+    CUDA graph and timed with CUDA events (maximum over ranks). With ``world`` > 1 the
+    decoder is tensor-parallel: heads, FFN and vocabulary split over the ranks, two
+    exchanges per layer (each rank stores its partial rows into the others' buffers over
+    NVLink; one kernel joins them with the residual add and RMSNorm) and one for the
+    greedy choice, all inside the graph; tokens/s counts the N tokens the whole job
+    makes per step (total work fixed: strong scaling). Reported beside the GEMM line."""
     import torch
-    from moat_b200.decode import DecoderConfig, Int4Decoder
+    from moat_b200.decode import DecoderConfig, Int4Decoder, timed_decode
     cfg = DecoderConfig()
     N, P = 16, 512
-    dec = Int4Decoder(cfg, N, device=dev, seed=SEED + 5)
-    dec.fill_prompt_cache(P, seed=SEED + 6)
-    g = torch.Generator(device=dev)
-    g.manual_seed(SEED + 7)
-    dec.ids.copy_(torch.randint(0, cfg.vocab, (N,), generator=g, device=dev, dtype=torch.int32))
-    dec.step(dec.ids)  # eager step: plans and tensor maps cached for the capture
-    dec.capture()
-    for _ in range(3):
-        dec.step_graphed()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        dec.step_graphed()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
-    err = int(dec.err.item())
-    wbytes = sum(sum(int(lw[k].numel()) for k in ("wqkv", "wo", "wgu", "wd")) for lw in dec.layers) \
-        + int(dec.lm_head.numel())
-    kv = 2 * cfg.layers * N * cfg.heads * cfg.head_dim * 2 * (P + 5 + steps // 2)  # mean cache length
+    dec = Int4Decoder(cfg, N, device=dev, seed=SEED + 5, rank=rank, world=world)
+    try:
+        dec.fill_prompt_cache(P, seed=SEED + 6)
+        g = torch.Generator(device=dev)
+        g.manual_seed(SEED + 7)
+        dec.ids.copy_(torch.randint(0, cfg.vocab, (N,), generator=g, device=dev, dtype=torch.int32))
+        ms = timed_decode(dec, steps, warmup=3, graph=True)
+        err = int(dec.err.item())
+        wbytes = sum(sum(int(lw[k].numel()) for k in ("wqkv", "wo", "wgu", "wd")) for lw in dec.layers) \
+            + int(dec.lm_head.numel())
+        kv = 2 * cfg.layers * N * dec.Hl * cfg.head_dim * 2 * (P + 5 + steps // 2)  # mean cache length
+        tot = torch.tensor([float(wbytes + kv), float(err)], dtype=torch.float64, device=dev)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(tot)
+        step_bytes, err = float(tot[0].item()), int(tot[1].item())
+    finally:
+        dec.close()  # graph and exchange buffers go before the process group
     del dec
     torch.cuda.empty_cache()
     return {"workload": "BASELINE config 5: 24-layer INT4 decoder, hidden 2048, 16x128 heads, FFN 5504, "
                         "vocab 151936; 16 traces, 512-position cache, greedy", "metric": "decode tok/s",
             "tok_per_s": N / ms * 1e3, "ms_per_step": ms, "steps": steps, "graph": True,
-            "bytes_per_step": wbytes + kv, "GBps": (wbytes + kv) / ms / 1e6, "device_error_bits": err,
+            "tensor_parallel": world, "scaling": "strong" if world > 1 else None,
+            "exchange": "NVLink peer stores (mb_peer_add_rmsnorm, mb_peer_argmax)" if world > 1 else None,
+            "bytes_per_step": step_bytes, "GBps": step_bytes / ms / 1e6, "device_error_bits": err,
             "data": "synthetic (random-init weights quantized to INT4; KV cache seeded N(0,1))"}
 
 

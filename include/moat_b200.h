@@ -44,6 +44,7 @@ extern "C" {
 /* Device-side error word bits (written to a caller-provided device word). */
 #define MB_DEVERR_TIMEOUT 1u /* a bounded wait gave up */
 #define MB_DEVERR_INDEX 2u   /* a device-side index (token id, position) was out of range */
+#define MB_DEVERR_NONFINITE 4u /* a sampled row had a non-finite (scaled) maximum logit */
 
 #define MB_ABI_VERSION 1
 
@@ -237,6 +238,82 @@ int32_t mb_swiglu(const uint16_t* gu, int32_t N, int32_t F, uint16_t* a, void* s
  * counts as the largest, like numpy.argmax (greedy sampling, batch_generator.py:203-206,
  * 224-227). */
 int32_t mb_argmax_f16(const uint16_t* logits, int32_t N, int32_t V, int32_t* ids, void* stream);
+
+/* Tensor-parallel greedy choice over a column-split vocabulary (the lm_head shards
+ * of a Megatron split; the reference decodes on one device, batch_generator.py:203-206).
+ * keys[n] = (c << 32) | (0xFFFFFFFF - (col0 + j)) for the largest logits[n, j] of this
+ * shard, c an order-preserving 16-bit code of the fp16 value (NaN largest, -0 == +0),
+ * so the int64 MAX over all shards (one all-reduce) is the global argmax with ties to
+ * the first column, exactly as mb_argmax_f16 over the whole row. */
+int32_t mb_argmax_key_f16(const uint16_t* logits, int32_t N, int32_t V, int32_t col0, int64_t* keys, void* stream);
+
+/* ids[n] = the column encoded in the combined keys[n] of mb_argmax_key_f16. */
+int32_t mb_argmax_keys_to_ids(const int64_t* keys, int32_t N, int32_t* ids, void* stream);
+
+/* ---- Tensor-parallel exchanges over NVLink peer memory -------------------------
+ * The reference runs on one device; these entry points join the Megatron shards of
+ * its decode step (transformer.py:148-158 residual + RMSNorm after o_proj and down;
+ * batch_generator.py:203-206 greedy choice after lm_head) without a library
+ * collective: each rank stores its rows into the other ranks' exchange buffers
+ * (CUDA IPC mappings, plain peer stores, no multicast), raises a release flag and
+ * waits, bounded by timeout_ns, for every rank's rows. A wait that expires sets
+ * MB_DEVERR_TIMEOUT in dev_err; the outputs of that call are then undefined.
+ * bufs[q] is rank q's exchange buffer as mapped in this process (bufs[rank] its own),
+ * each of mb_peer_buffer_bytes(max_rows, D) bytes, zeroed before the first call.
+ * state is a per-rank DEVICE array of 2 uint32 per exchange kind (zeroed once; the
+ * epoch lives there, so a captured graph replays). Every rank must make the same
+ * sequence of calls, each rank on its own GPU. */
+#define MB_IPC_HANDLE_BYTES 64
+
+/* Bytes of one exchange buffer for up to max_rows (<= 64) rows of D (multiple of 8)
+ * fp16 values and up to 8 ranks; 0 for unsupported sizes. */
+size_t mb_peer_buffer_bytes(int32_t max_rows, int32_t D);
+
+/* cudaMalloc(bytes), zero it and write its CUDA IPC handle (MB_IPC_HANDLE_BYTES). */
+int32_t mb_ipc_alloc(size_t bytes, void** ptr, uint8_t* handle);
+/* Map another process's buffer from its IPC handle (peer access enabled). */
+int32_t mb_ipc_open(const uint8_t* handle, void** ptr);
+int32_t mb_ipc_close(void* ptr);
+int32_t mb_ipc_free(void* ptr);
+
+/* Row-parallel join fused with the next residual add and RMSNorm: with P_q the
+ * partial [N, D] fp16 of rank q, y = fp16(sum over q = 0..world-1 of P_q, in rank order
+ * in fp32), x += y (fp32 [N, D]) and h = fp16(x * rsqrt(mean(x^2) + eps) * w) as
+ * mb_add_rmsnorm; identical x and h on every rank. slot_elems >= N * D (the max_rows
+ * * D the buffers were sized for). */
+int32_t mb_peer_add_rmsnorm(void* const* bufs, int32_t world, int32_t rank, int64_t slot_elems, int64_t timeout_ns,
+                            const uint16_t* partial, float* x, const float* w, int32_t N, int32_t D, float eps,
+                            uint16_t* h, uint32_t* state, uint32_t* dev_err, void* stream);
+
+/* Greedy choice over a column-split vocabulary: this rank holds logits [N, V] of
+ * columns [col0, col0 + V); ids[n] = the global first index of the largest logit over
+ * all ranks (NaN largest, -0 == +0), as mb_argmax_f16 over the whole row. */
+int32_t mb_peer_argmax(void* const* bufs, int32_t world, int32_t rank, int64_t slot_elems, int64_t timeout_ns,
+                       const uint16_t* logits, int32_t N, int32_t V, int32_t col0, int32_t* ids, uint32_t* state,
+                       uint32_t* dev_err, void* stream);
+
+/* ---- Batched sampling (BatchedRolloutCoordinator.sample_tokens, NumPy branch,
+ * batch_generator.py:187-253) ----------------------------------------------------
+ * logits [N, V] fp16 (logits_f32 = 0) or fp32 (1), device. temperature <= 0: greedy,
+ * tokens[n] = first index of the largest logit, logprobs[n] = fp16(log p) with p the
+ * fp16 LUT softmax (safe_softmax_lut, attention.py:97-134) of the raw row.
+ * temperature > 0: s = logits / max(T, 1e-5) (fp16 logits: fp16 quotient by fp16(T)),
+ * p = fp16 LUT softmax of s; the k = min(top_k, V) largest p, ordered by (p desc,
+ * column asc), renormalised; the token is the first candidate whose running fp32 sum
+ * exceeds u * total; logprobs[n] = log(max(p_token, 1e-10)) (fp32). u is uniforms[n]
+ * (device, [0, 1)) if given, else the top 24 bits of splitmix64(splitmix64(seed ^
+ * counter * 0xD1B54A32D192ED03) + n) * 2^-24, counter = rng_state[0]. Every call
+ * advances rng_state[0] by one on the device (rng_state: 2 uint32, zeroed once), so a
+ * captured graph draws fresh values each replay. The table is the exp LUT
+ * (ExponentialLUT, attention.py:21-90; the reference sampler uses range_max 10), at
+ * most 32768 entries. top_k in [1, 64] (the reference uses 50). A row whose (scaled)
+ * maximum is not finite (the reference raises) sets MB_DEVERR_NONFINITE, returns its
+ * argmax and a NaN logprob. The workspace holds N * V uint16 table indices. */
+size_t mb_sample_workspace_size(int32_t N, int32_t V);
+int32_t mb_sample_tokens(const void* logits, int32_t logits_f32, int32_t N, int32_t V, float temperature,
+                         int32_t top_k, const uint16_t* table, int32_t size, float range_max, const float* uniforms,
+                         uint64_t seed, uint32_t* rng_state, int32_t* tokens, float* logprobs, void* workspace,
+                         size_t workspace_bytes, uint32_t* dev_err, void* stream);
 
 /* pos[n] += 1 on the device (the next decode step's positions; no reference
  * counterpart: keeps a captured step replayable). */

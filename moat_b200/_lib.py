@@ -45,7 +45,21 @@ SIGNATURES = {
     "mb_rope_append": (_c_i32, [_vp, _c_i32, _c_i32, _c_i32, _vp, _vp, _c_i32, _vp, _vp, _vp, _vp, _vp]),
     "mb_swiglu": (_c_i32, [_vp, _c_i32, _c_i32, _vp, _vp]),
     "mb_argmax_f16": (_c_i32, [_vp, _c_i32, _c_i32, _vp, _vp]),
+    "mb_argmax_key_f16": (_c_i32, [_vp, _c_i32, _c_i32, _c_i32, _vp, _vp]),
+    "mb_argmax_keys_to_ids": (_c_i32, [_vp, _c_i32, _vp, _vp]),
     "mb_advance_positions": (_c_i32, [_vp, _c_i32, _vp]),
+    "mb_peer_buffer_bytes": (_c_sz, [_c_i32, _c_i32]),
+    "mb_ipc_alloc": (_c_i32, [_c_sz, _vp, _vp]),
+    "mb_ipc_open": (_c_i32, [_vp, _vp]),
+    "mb_ipc_close": (_c_i32, [_vp]),
+    "mb_ipc_free": (_c_i32, [_vp]),
+    "mb_peer_add_rmsnorm": (_c_i32, [_vp, _c_i32, _c_i32, _c_i64, _c_i64, _vp, _vp, _vp, _c_i32, _c_i32, _c_f, _vp,
+                                     _vp, _vp, _vp]),
+    "mb_peer_argmax": (_c_i32, [_vp, _c_i32, _c_i32, _c_i64, _c_i64, _vp, _c_i32, _c_i32, _c_i32, _vp, _vp, _vp,
+                                _vp]),
+    "mb_sample_workspace_size": (_c_sz, [_c_i32, _c_i32]),
+    "mb_sample_tokens": (_c_i32, [_vp, _c_i32, _c_i32, _c_i32, _c_f, _c_i32, _vp, _c_i32, _c_f, _vp, ctypes.c_uint64,
+                                  _vp, _vp, _vp, _vp, _c_sz, _vp, _vp]),
     "mb_decode_attn_noalloc": (_c_i32, [_vp, _vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _c_i32, _c_f, _vp, _c_i32,
                                         _c_f, _vp]),
 }

@@ -161,6 +161,52 @@ __global__ void __launch_bounds__(kRowBlock) k_argmax(const uint16_t* __restrict
   if (threadIdx.x == 0) ids[n] = bi[0] == 0x7fffffff ? 0 : bi[0];
 }
 
+// Order-preserving 16-bit code of an fp16 logit under the argmax rules above: every
+// NaN is the largest code, -0 and +0 share one code (equal values), and otherwise a
+// larger value has a larger code.
+__device__ __forceinline__ uint32_t argmax_code(uint16_t h) {
+  if ((h & 0x7C00u) == 0x7C00u && (h & 0x03FFu)) return 0xFFFFu;
+  if (h == 0x8000u) h = 0;
+  return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
+}
+
+// One row shard of a column-split vocabulary: the shard's best logit as a 64-bit key,
+// code << 32 | (0xFFFFFFFF - global column). The largest key over all shards is the
+// global argmax with ties to the first column, so the shards combine with one integer
+// MAX all-reduce.
+__global__ void __launch_bounds__(kRowBlock) k_argmax_key(const uint16_t* __restrict__ logits, int V, int col0,
+                                                          int64_t* __restrict__ keys) {
+  __shared__ unsigned long long best_w[kRowBlock / 32];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int n = blockIdx.x;
+  const uint16_t* row = logits + static_cast<int64_t>(n) * V;
+  unsigned long long best = 0;
+  for (int c = threadIdx.x; c < V; c += kRowBlock) {
+    const unsigned long long key = (static_cast<unsigned long long>(argmax_code(row[c])) << 32) |
+                                   (0xFFFFFFFFull - static_cast<unsigned long long>(col0 + c));
+    best = key > best ? key : best;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) best_w[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kRowBlock / 32; ++w) best = best_w[w] > best ? best_w[w] : best;
+    keys[n] = static_cast<int64_t>(best);
+  }
+}
+
+__global__ void k_keys_to_ids(const int64_t* __restrict__ keys, int N, int32_t* __restrict__ ids) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n < N) ids[n] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(keys[n] & 0xFFFFFFFFll));
+}
+
 // pos[n] += 1 (the next step's position), on the device so a captured step can replay.
 __global__ void k_advance(int32_t* pos, int N) {
   pdl_wait();
@@ -215,6 +261,20 @@ int32_t mb_argmax_f16(const uint16_t* logits, int32_t N, int32_t V, int32_t* ids
   if (!logits || !ids) return MB_ERR_NULL;
   if (N < 1 || V < 1) return MB_ERR_ARGS;
   return launch_with_pdl(k_argmax, dim3(N), dim3(kRowBlock), 0, static_cast<cudaStream_t>(stream), logits, V, ids);
+}
+
+int32_t mb_argmax_key_f16(const uint16_t* logits, int32_t N, int32_t V, int32_t col0, int64_t* keys, void* stream) {
+  if (!logits || !keys) return MB_ERR_NULL;
+  if (N < 1 || V < 1 || col0 < 0 || static_cast<int64_t>(col0) + V > 0x7FFFFFFFll) return MB_ERR_ARGS;
+  return launch_with_pdl(k_argmax_key, dim3(N), dim3(kRowBlock), 0, static_cast<cudaStream_t>(stream), logits, V,
+                         col0, keys);
+}
+
+int32_t mb_argmax_keys_to_ids(const int64_t* keys, int32_t N, int32_t* ids, void* stream) {
+  if (!keys || !ids) return MB_ERR_NULL;
+  if (N < 1) return MB_ERR_ARGS;
+  return launch_with_pdl(k_keys_to_ids, dim3((N + 127) / 128), dim3(128), 0, static_cast<cudaStream_t>(stream), keys,
+                         N, ids);
 }
 
 int32_t mb_advance_positions(int32_t* pos, int32_t N, void* stream) {

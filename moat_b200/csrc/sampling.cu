@@ -1,0 +1,379 @@
+// Batched token sampling with the exp-LUT softmax on B200 (sm_100a).
+//
+// Reference: BatchedRolloutCoordinator.sample_tokens, NumPy branch
+// (antigravity-engine/src/batch_generator.py:187-253), with safe_softmax_lut
+// (attention.py:97-134) on a 32,768-entry table over [-10, 0]:
+//   greedy (T <= 0) : token = first index of the largest logit; logprob =
+//                     fp16(log(p_token)), p = the fp16 LUT softmax of the raw logits;
+//   T > 0           : s = logits / max(T, 1e-5) (fp16 logits: fp16 quotient of the fp32
+//                     values by fp16(T); fp32 logits: fp32 quotient), p = fp16 LUT
+//                     softmax of s, the top-k (k = min(50, V)) of p renormalised, one
+//                     draw; logprob = log(max(p_token, 1e-10)) in fp32.
+// Defined where the reference leaves it open: the row sum of the fp16 table values is
+// exact (integer units of 2^-24) and rounded to fp32 once; the top-k set and its order
+// are by (p descending, column ascending); the draw takes the first candidate whose
+// running fp32 sum exceeds u * total for a uniform u in [0, 1) (given, or the
+// counter-based SplitMix64 stream below). A row whose (scaled) maximum is not finite
+// makes the reference raise; here it sets MB_DEVERR_NONFINITE, token = the argmax,
+// logprob = NaN.
+//
+// One CTA of 1024 threads per row:
+//   A  max and first argmax of the raw logits (the scaled maximum is the scaled value
+//      at that column: the scaling is monotone);
+//   B  per element the table index of (s - max) into a uint16 scratch row, and the
+//      exact sum of the table values (uint64);
+//   p16 table: for every table index its fp16 probability fp16(e / sum), in shared
+//      memory (the probability of an element is a function of its index alone);
+//   C, D  256-bin histograms of the high, then the low byte of the fp16 probability
+//      bits give the k-th largest probability t;
+//   E  every column with p > t, and the first (k - #{p > t}) columns with p == t in
+//      column order (per-thread contiguous ranges and a block prefix sum);
+//   a warp ranks the <= 64 candidate keys (p << 32 | ~column), thread 0 draws.
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace mb {
+
+constexpr int kSampBlock = 1024;
+constexpr int kSampMaxK = 64;
+
+__device__ __forceinline__ int samp_lut_index(float x, float step, int size) {
+  float f = __fdiv_rn(fabsf(x), step);
+  f = fminf(fmaxf(f, 0.0f), static_cast<float>(size - 1));
+  return static_cast<int>(f);
+}
+
+struct SampArgs {
+  const void* logits;
+  int f32;  // 1: fp32 logits, 0: fp16
+  int V;
+  int scale;    // 0: greedy (raw logits)
+  float tdiv;   // fp32(max(T, 1e-5)), or its fp16 rounding for fp16 logits
+  int k;
+  const uint16_t* table;
+  int size;
+  float step;
+  const float* uniforms;  // [N] or null
+  unsigned long long seed;
+  uint32_t* rng_state;  // {counter, arrivals}
+  int32_t* tokens;
+  float* logprobs;
+  uint16_t* scratch;  // [N][V] table indices
+  uint32_t* err;
+};
+
+__device__ __forceinline__ float samp_raw(const SampArgs& a, int64_t i) {
+  return a.f32 ? __ldg(static_cast<const float*>(a.logits) + i)
+               : __half2float(__ushort_as_half(__ldg(static_cast<const uint16_t*>(a.logits) + i)));
+}
+
+__device__ __forceinline__ float samp_scaled(const SampArgs& a, float x) {
+  if (!a.scale) return x;
+  const float q = __fdiv_rn(x, a.tdiv);
+  return a.f32 ? q : __half2float(__float2half_rn(q));
+}
+
+__device__ __forceinline__ unsigned long long splitmix64(unsigned long long z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Block reductions (1024 threads = 32 warps); `red` holds 32 slots.
+__device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v, unsigned long long* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  unsigned long long t = 0;
+#pragma unroll
+  for (int w = 0; w < kSampBlock / 32; ++w) t += red[w];
+  return t;
+}
+
+__device__ __forceinline__ unsigned long long block_max_u64(unsigned long long v, unsigned long long* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const unsigned long long x = __shfl_xor_sync(0xffffffffu, v, o);
+    v = x > v ? x : v;
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  unsigned long long t = 0;
+#pragma unroll
+  for (int w = 0; w < kSampBlock / 32; ++w) t = red[w] > t ? red[w] : t;
+  return t;
+}
+
+// Order-preserving 32-bit code of an fp32 value for the argmax: NaN largest, -0 == +0.
+__device__ __forceinline__ uint32_t samp_code(float v) {
+  if (v != v) return 0xFFFFFFFFu;
+  uint32_t b = __float_as_uint(v);
+  if (b == 0x80000000u) b = 0;
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Walks the 256 bins from the top: the bin holding the `need`-th largest element.
+// Returns the bin and writes the count of elements in higher bins.
+__device__ __forceinline__ int pick_bin(const uint32_t* hist, uint32_t need, uint32_t* above) {
+  uint32_t cum = 0;
+  for (int b = 255; b >= 0; --b) {
+    if (cum + hist[b] >= need) {
+      *above = cum;
+      return b;
+    }
+    cum += hist[b];
+  }
+  *above = cum;
+  return 0;
+}
+
+__global__ void __launch_bounds__(kSampBlock) k_sample(SampArgs a) {
+  extern __shared__ uint16_t ptab[];  // [size] fp16 probability bits per table index
+  __shared__ unsigned long long red[kSampBlock / 32];
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t scan[kSampBlock / 32];
+  __shared__ unsigned long long cand[kSampMaxK];
+  __shared__ unsigned long long sorted[kSampMaxK];
+  __shared__ uint32_t ncand;
+  __shared__ uint32_t sel[4];  // bin, above, threshold, c_gt
+  pdl_wait();
+  pdl_launch_dependents();
+  const int n = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int64_t row = static_cast<int64_t>(n) * a.V;
+  uint16_t* srow = a.scratch + row;
+
+  // A: first index of the largest raw logit (NaN largest)
+  unsigned long long best = 0;
+  for (int c = tid; c < a.V; c += kSampBlock) {
+    const unsigned long long key =
+        (static_cast<unsigned long long>(samp_code(samp_raw(a, row + c))) << 32) | (0xFFFFFFFFull - c);
+    best = key > best ? key : best;
+  }
+  best = block_max_u64(best, red);
+  const int amax = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+  const float m = samp_scaled(a, samp_raw(a, row + amax));
+  const uint32_t counter = *reinterpret_cast<volatile uint32_t*>(a.rng_state);
+  if (!isfinite(m)) {  // the reference raises on a non-finite maximum
+    if (tid == 0) {
+      if (a.err) atomicOr(a.err, MB_DEVERR_NONFINITE);
+      a.tokens[n] = amax;
+      a.logprobs[n] = __int_as_float(0x7fc00000);
+    }
+  } else {
+    // B: table indices and the exact sum of the table values
+    unsigned long long acc = 0;
+    for (int c = tid; c < a.V; c += kSampBlock) {
+      const int j = samp_lut_index(samp_scaled(a, samp_raw(a, row + c)) - m, a.step, a.size);
+      if (a.scale) srow[c] = static_cast<uint16_t>(j);
+      const float e = __half2float(__ushort_as_half(__ldg(a.table + (a.size - 1 - j))));
+      acc += static_cast<unsigned long long>(e * 16777216.0f);  // exact: e is a multiple of 2^-24, <= 1
+    }
+    acc = block_sum_u64(acc, red);
+    float sum = __ull2float_rn(acc) * 5.9604644775390625e-8f;  // * 2^-24, exact
+    if (!(sum > 0.0f)) sum = 1.0f;
+    if (!a.scale) {
+      if (tid == 0) {
+        const float e0 = __half2float(__ushort_as_half(__ldg(a.table + (a.size - 1))));
+        const float p = __half2float(__float2half_rn(__fdiv_rn(e0, sum)));
+        a.tokens[n] = amax;
+        a.logprobs[n] = __half2float(__float2half_rn(logf(p)));
+      }
+    } else {
+      // probability bits per table index
+      for (int j = tid; j < a.size; j += kSampBlock) {
+        const float e = __half2float(__ushort_as_half(__ldg(a.table + (a.size - 1 - j))));
+        ptab[j] = __half_as_ushort(__float2half_rn(__fdiv_rn(e, sum)));
+      }
+      for (int b = tid; b < 256; b += kSampBlock) hist[b] = 0;
+      __syncthreads();
+      const uint32_t k = static_cast<uint32_t>(a.k);
+      // C: high byte histogram
+      for (int base = 0; base < a.V; base += kSampBlock) {
+        const int c = base + tid;
+        const int bin = c < a.V ? (ptab[__ldcg(srow + c)] >> 8) : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, bin);
+        if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+      }
+      __syncthreads();
+      if (tid == 0) {
+        uint32_t above;
+        sel[0] = static_cast<uint32_t>(pick_bin(hist, k, &above));
+        sel[1] = above;
+      }
+      __syncthreads();
+      const uint32_t hb = sel[0], above_hi = sel[1];
+      for (int b = tid; b < 256; b += kSampBlock) hist[b] = 0;
+      __syncthreads();
+      // D: low byte histogram inside the high bin
+      for (int base = 0; base < a.V; base += kSampBlock) {
+        const int c = base + tid;
+        int bin = -1;
+        if (c < a.V) {
+          const uint32_t p = ptab[__ldcg(srow + c)];
+          if ((p >> 8) == hb) bin = static_cast<int>(p & 0xFFu);
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, bin);
+        if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+      }
+      __syncthreads();
+      if (tid == 0) {
+        uint32_t above;
+        const int lo = pick_bin(hist, k - above_hi, &above);
+        sel[2] = (hb << 8) | static_cast<uint32_t>(lo);
+        sel[3] = above_hi + above;
+        ncand = 0;
+      }
+      __syncthreads();
+      const uint32_t t = sel[2], c_gt = sel[3];
+      const uint32_t need = k - c_gt;  // >= 1 columns with p == t, the first ones by column
+      // E: contiguous column range per thread, in column order
+      const int chunk = (a.V + kSampBlock - 1) / kSampBlock;
+      const int c0 = min(a.V, tid * chunk), c1 = min(a.V, c0 + chunk);
+      uint32_t ties = 0;
+      for (int c = c0; c < c1; ++c) {
+        const uint32_t p = ptab[__ldcg(srow + c)];
+        if (p > t) {
+          const uint32_t slot = atomicAdd(&ncand, 1u);
+          if (slot < kSampMaxK) cand[slot] = (static_cast<unsigned long long>(p) << 32) | (0xFFFFFFFFull - c);
+        } else if (p == t) {
+          ++ties;
+        }
+      }
+      // exclusive prefix of the tie counts over threads (thread order = column order)
+      uint32_t incl = ties;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += x;
+      }
+      if (lane == 31) scan[tid >> 5] = incl;
+      __syncthreads();
+      if (tid < 32) {
+        const uint32_t v = scan[tid];
+        uint32_t s2 = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t x = __shfl_up_sync(0xffffffffu, s2, o);
+          if (lane >= o) s2 += x;
+        }
+        scan[tid] = s2 - v;  // exclusive over warps
+      }
+      __syncthreads();
+      uint32_t rank = scan[tid >> 5] + incl - ties;
+      for (int c = c0; c < c1 && rank < need; ++c) {
+        if (ptab[__ldcg(srow + c)] == t) {
+          const uint32_t slot = c_gt + rank;
+          if (slot < kSampMaxK) cand[slot] = (static_cast<unsigned long long>(t) << 32) | (0xFFFFFFFFull - c);
+          ++rank;
+        }
+      }
+      __syncthreads();
+      // rank the k candidate keys (distinct: the column is part of the key)
+      if (tid < 32) {
+        for (uint32_t i = tid; i < k; i += 32) {
+          const unsigned long long key = cand[i];
+          uint32_t r = 0;
+          for (uint32_t j = 0; j < k; ++j) r += cand[j] > key ? 1u : 0u;
+          sorted[r] = key;
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        float u;
+        if (a.uniforms) {
+          u = a.uniforms[n];
+        } else {
+          const unsigned long long base =
+              splitmix64(a.seed ^ (static_cast<unsigned long long>(counter) * 0xD1B54A32D192ED03ull));
+          u = static_cast<float>(splitmix64(base + static_cast<unsigned long long>(n)) >> 40) *
+              5.9604644775390625e-8f;
+        }
+        float total = 0.0f;
+        for (uint32_t i = 0; i < k; ++i)
+          total += __half2float(__ushort_as_half(static_cast<uint16_t>(sorted[i] >> 32)));
+        uint32_t pick = k - 1;
+        if (total > 0.0f) {
+          const float target = u * total;
+          float run = 0.0f;
+          for (uint32_t i = 0; i < k; ++i) {
+            run += __half2float(__ushort_as_half(static_cast<uint16_t>(sorted[i] >> 32)));
+            if (run > target) {
+              pick = i;
+              break;
+            }
+          }
+        } else {
+          pick = min(static_cast<uint32_t>(floorf(u * static_cast<float>(k))), k - 1);
+        }
+        const unsigned long long key = sorted[pick];
+        const float p = __half2float(__ushort_as_half(static_cast<uint16_t>(key >> 32)));
+        a.tokens[n] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
+        a.logprobs[n] = logf(fmaxf(p, 1e-10f));
+      }
+    }
+  }
+  // the last CTA advances the random stream's counter (read by the next call)
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(a.rng_state + 1, 1u) == gridDim.x - 1) {
+      a.rng_state[1] = 0;
+      a.rng_state[0] = counter + 1;
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace mb
+
+using namespace mb;
+
+extern "C" {
+
+size_t mb_sample_workspace_size(int32_t N, int32_t V) {
+  if (N < 1 || V < 1) return 0;
+  return (static_cast<size_t>(N) * V * sizeof(uint16_t) + 255) / 256 * 256;
+}
+
+int32_t mb_sample_tokens(const void* logits, int32_t logits_f32, int32_t N, int32_t V, float temperature,
+                         int32_t top_k, const uint16_t* table, int32_t size, float range_max, const float* uniforms,
+                         uint64_t seed, uint32_t* rng_state, int32_t* tokens, float* logprobs, void* workspace,
+                         size_t workspace_bytes, uint32_t* dev_err, void* stream) {
+  if (!logits || !table || !rng_state || !tokens || !logprobs || !workspace) return MB_ERR_NULL;
+  if (N < 1 || V < 1 || V > 0x7FFFFFFE || size < 2 || size > 32768 || !(range_max > 0.0f) || top_k < 1 ||
+      top_k > kSampMaxK || (logits_f32 != 0 && logits_f32 != 1))
+    return MB_ERR_ARGS;
+  if (workspace_bytes < mb_sample_workspace_size(N, V)) return MB_ERR_WORKSPACE;
+  SampArgs a;
+  a.logits = logits;
+  a.f32 = logits_f32;
+  a.V = V;
+  a.scale = temperature > 0.0f ? 1 : 0;
+  const float t32 = fmaxf(temperature, 1e-5f);
+  a.tdiv = logits_f32 ? t32 : __half2float(__float2half_rn(t32));
+  a.k = top_k < V ? top_k : V;
+  a.table = table;
+  a.size = size;
+  a.step = static_cast<float>(static_cast<double>(range_max) / (size - 1));
+  a.uniforms = uniforms;
+  a.seed = seed;
+  a.rng_state = rng_state;
+  a.tokens = tokens;
+  a.logprobs = logprobs;
+  a.scratch = static_cast<uint16_t*>(workspace);
+  a.err = dev_err;
+  const size_t smem = static_cast<size_t>(size) * sizeof(uint16_t);
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+          cudaSuccess)
+    return MB_ERR_LAUNCH;
+  return launch_with_pdl(k_sample, dim3(N), dim3(kSampBlock), smem, static_cast<cudaStream_t>(stream), a);
+}
+
+}  // extern "C"

@@ -1,4 +1,4 @@
-"""INT4 decoder step: greedy decode of N parallel traces through a LLaMA-style model.
+"""INT4 decoder step: decode of N parallel traces through a LLaMA-style model.
 
 The model is the reference's ``TinyLlamaModel`` architecture
 (``antigravity-engine/src/transformer.py:161-225``: RMSNorm, RoPE, attention with a
@@ -17,6 +17,22 @@ x 128, FFN 5504, vocab 151936, multi-head attention). Layout per layer, with
 * KV caches ``[N, H, max_len, head_dim]`` fp16 per layer.
 
 The residual stream stays fp32; each GEMM input is rounded to fp16 once.
+
+Tensor parallelism (``rank``/``world``, one process per GPU): the Megatron split of
+``tp_shards``. q/k/v columns, o_proj rows and the KV cache of a head range; gate/up
+columns and down rows of an FFN range; lm_head columns of a vocabulary range. Every
+rank draws the whole weights from the same random stream as one GPU and keeps its
+slice, so the shards hold exactly the one-GPU model's codes and scales. The two
+row-parallel partial products of a layer are joined by ``exchange="peer"`` (one
+kernel per join: peer stores over NVLink, then the residual add and RMSNorm; the
+default) or ``"nccl"`` (``all_reduce``, then ``mb_add_rmsnorm``); the greedy choice
+over the split vocabulary is one 64-bit key per shard, maximised across ranks.
+
+``temperature > 0`` (one GPU) replaces the greedy choice by ``mb_sample_tokens``: a
+draw from the top-50 of the exp-LUT softmax of the scaled logits, as the reference's
+``sample_tokens`` (``batch_generator.py:187-253``), with the random stream's counter
+on the device so the captured step keeps drawing fresh values; ``logprobs`` holds
+each trace's log-probability of its token.
 """
 
 from __future__ import annotations
@@ -55,11 +71,29 @@ def rope_table(head_dim: int, max_len: int, theta: float):
     return t.view_as_real(cis).contiguous()
 
 
+def tp_shards(cfg: DecoderConfig, world: int):
+    """Megatron split of the decoder over ``world`` GPUs: per rank its head range
+    (q/k/v columns, o_proj rows, KV cache), its FFN range (gate/up columns, down rows)
+    and its vocabulary range (lm_head columns). FFN and vocabulary ranges are cut on
+    128-column boundaries where the size allows (whole quantization groups, and widths
+    the fast GEMM plan takes), else on 32-column group boundaries."""
+    from .dist import column_bounds, head_bounds
+
+    def cols(M):
+        if world == 1:
+            return [(0, M)]
+        return column_bounds(M, world, group=128 if M % 128 == 0 and M // 128 >= world else 32)
+
+    return {"heads": head_bounds(cfg.heads, world), "ffn": cols(cfg.ffn), "vocab": cols(cfg.vocab)}
+
+
 class Int4Decoder:
-    """Random-init INT4 decoder on one GPU, for N traces decoding in lockstep."""
+    """Random-init INT4 decoder for N traces decoding in lockstep, on one GPU or
+    tensor-parallel over ``world`` GPUs (this process being ``rank``)."""
 
     def __init__(self, cfg: DecoderConfig, n_traces: int, device="cuda:0", seed: int = 0, std: float = 0.02,
-                 keep_dense: bool = False):
+                 keep_dense: bool = False, rank: int = 0, world: int = 1, group=None, exchange: str = "peer",
+                 exchange_timeout_s: float = 10.0, temperature: float = 0.0, sample_seed: int = 0):
         t = _lib.require_cuda()
         from .attention import ExponentialLUT
         from .dequant import quantize_to_superblocks
@@ -68,50 +102,82 @@ class Int4Decoder:
         D, H, dh, F, V = cfg.hidden, cfg.heads, cfg.head_dim, cfg.ffn, cfg.vocab
         if H * dh != D:
             raise ValueError("heads * head_dim must equal hidden")
+        if not 0 <= rank < world:
+            raise ValueError(f"rank {rank} outside world {world}")
+        if exchange not in ("peer", "nccl"):
+            raise ValueError("exchange must be 'peer' or 'nccl'")
+        if temperature > 0 and world > 1:
+            raise NotImplementedError("temperature sampling runs on one GPU (the vocabulary is not split)")
+        self.rank, self.world, self.group = rank, world, group
+        self.exchange, self.peer, self.exchange_timeout_s = exchange, None, exchange_timeout_s
+        self.temperature = float(temperature)
+        self.shards = tp_shards(cfg, world)
+        sh = {k: v[rank] for k, v in self.shards.items()}
+        (h0, h1), (f0, f1), (v0, v1) = sh["heads"], sh["ffn"], sh["vocab"]
+        self.Hl, self.Fl, self.Vl, self.v0 = h1 - h0, f1 - f0, v1 - v0, v0
+        Hl, Fl, Vl = self.Hl, self.Fl, self.Vl
+        Dl = Hl * dh
+        self.head_range = (h0, h1)
         g = t.Generator(device=self.dev)
         g.manual_seed(seed)
         self.dense = [] if keep_dense else None
 
-        def int4(K, M):
+        def int4(K, M, cols=None, rows=None):
+            # the whole [K, M] weight is drawn on every rank (the same random stream as
+            # one GPU), then this rank's columns / rows are quantized: whole 32-wide
+            # groups, so its codes and scales equal the unsplit weight's
             w = t.randn((K, M), generator=g, device=self.dev, dtype=t.float32) * std
             if self.dense is not None:
                 self.dense.append(w.cpu())
-            sb = quantize_to_superblocks(w.reshape(-1))
+            if cols is not None and world > 1:
+                w = t.cat([w[:, c0:c1] for c0, c1 in cols], dim=1)
+            if rows is not None and world > 1:
+                w = w[rows[0]:rows[1]]
+            sb = quantize_to_superblocks(w.contiguous().reshape(-1))
             del w
             return sb
 
+        qkv_cols = [(j * D + h0 * dh, j * D + h1 * dh) for j in range(3)]
+        gu_cols = [(f0, f1), (F + f0, F + f1)]
         self.layers = []
         for _ in range(cfg.layers):
             self.layers.append({
-                "wqkv": int4(D, 3 * D), "wo": int4(D, D), "wgu": int4(D, 2 * F), "wd": int4(F, D),
+                "wqkv": int4(D, 3 * D, cols=qkv_cols), "wo": int4(D, D, rows=(h0 * dh, h1 * dh)),
+                "wgu": int4(D, 2 * F, cols=gu_cols), "wd": int4(F, D, rows=(f0, f1)),
                 "attn_norm": (1.0 + 0.02 * t.randn((D,), generator=g, device=self.dev)).float(),
                 "ffn_norm": (1.0 + 0.02 * t.randn((D,), generator=g, device=self.dev)).float(),
             })
         self.final_norm = (1.0 + 0.02 * t.randn((D,), generator=g, device=self.dev)).float()
-        self.lm_head = int4(D, V)
+        self.lm_head = int4(D, V, cols=[(v0, v1)])
         self.embed = (t.randn((V, D), generator=g, device=self.dev) * std).half()
         self.cs = rope_table(dh, cfg.max_len, cfg.theta).to(self.dev)
         self.lut = ExponentialLUT(range_max=cfg.lut_range)
         self.table = self.lut.device_table(self.dev)
         N, L = n_traces, cfg.max_len
-        self.k_cache = [t.zeros((N, H, L, dh), dtype=t.float16, device=self.dev) for _ in range(cfg.layers)]
-        self.v_cache = [t.zeros((N, H, L, dh), dtype=t.float16, device=self.dev) for _ in range(cfg.layers)]
+        self.k_cache = [t.zeros((N, Hl, L, dh), dtype=t.float16, device=self.dev) for _ in range(cfg.layers)]
+        self.v_cache = [t.zeros((N, Hl, L, dh), dtype=t.float16, device=self.dev) for _ in range(cfg.layers)]
         f16, f32 = t.float16, t.float32
         self.x = t.empty((N, D), dtype=f32, device=self.dev)
         self.h = t.empty((N, D), dtype=f16, device=self.dev)
-        self.qkv = t.empty((N, 3 * D), dtype=f16, device=self.dev)
-        self.q = t.empty((N, H, dh), dtype=f16, device=self.dev)
-        self.att = t.empty((N, H, dh), dtype=f16, device=self.dev)
+        self.qkv = t.empty((N, 3 * Dl), dtype=f16, device=self.dev)
+        self.q = t.empty((N, Hl, dh), dtype=f16, device=self.dev)
+        self.att = t.empty((N, Hl, dh), dtype=f16, device=self.dev)
         self.o = t.empty((N, D), dtype=f16, device=self.dev)
-        self.gu = t.empty((N, 2 * F), dtype=f16, device=self.dev)
-        self.a = t.empty((N, F), dtype=f16, device=self.dev)
-        self.logits = t.empty((N, V), dtype=f16, device=self.dev)
+        self.gu = t.empty((N, 2 * Fl), dtype=f16, device=self.dev)
+        self.a = t.empty((N, Fl), dtype=f16, device=self.dev)
+        self.logits = t.empty((N, Vl), dtype=f16, device=self.dev)
+        self.keys = t.zeros((N,), dtype=t.int64, device=self.dev)
         self.ids = t.zeros((N,), dtype=t.int32, device=self.dev)
+        self.logprobs = t.zeros((N,), dtype=t.float32, device=self.dev)
         self.pos = t.zeros((N,), dtype=t.int32, device=self.dev)
         self.err = t.zeros((1,), dtype=t.int32, device=self.dev)
+        self.sampler = None
+        if self.temperature > 0:  # top-50 draw from the LUT softmax (range 10), device random stream
+            from .sampling import BatchSampler
+            self.sampler = BatchSampler(n_traces, V, device=self.dev, seed=sample_seed)
         self.length = 0  # positions filled so far (the same for every trace)
         self.graph = None
-        nb = int(lib().mb_decode_attn_workspace_size(N, H, L, dh))
+        nb = int(lib().mb_decode_attn_workspace_size(N, Hl, L, dh))
         self.ws = t.zeros(nb, dtype=t.uint8, device=self.dev)
         self.scale = float(np.float32(1.0 / np.sqrt(dh)))
 
@@ -119,21 +185,31 @@ class Int4Decoder:
     def fill_prompt_cache(self, length: int, seed: int = 1):
         """Seeded N(0,1) keys and values for the first ``length`` positions of every
         layer (a stand-in for the prompt's prefill; decode speed does not depend on the
-        cache contents), and sets the next position to ``length``."""
+        cache contents), and sets the next position to ``length``. A tensor-parallel
+        rank draws every head as one GPU does and keeps its own heads."""
         t = _lib.torch()
         if not 0 <= length < self.cfg.max_len:
             raise ValueError("prompt length must leave room to decode")
         g = t.Generator(device=self.dev)
         g.manual_seed(seed)
+        h0, h1 = self.head_range
+        full = None
+        if self.world > 1:
+            cfg = self.cfg
+            full = t.zeros((self.N, cfg.heads, cfg.max_len, cfg.head_dim), dtype=t.float16, device=self.dev)
         for kc, vc in zip(self.k_cache, self.v_cache):
-            kc[:, :, :length].normal_(generator=g)
-            vc[:, :, :length].normal_(generator=g)
+            for c in (kc, vc):
+                if full is None:
+                    c[:, :, :length].normal_(generator=g)
+                else:
+                    full[:, :, :length].normal_(generator=g)
+                    c.copy_(full[:, h0:h1])
         self.length = length
         self.pos.fill_(length)
 
     def step(self, ids):
-        """One decode step for all traces: token ids [N] (int32, device) in, the greedy
-        next ids [N] out (a device tensor, also kept in ``self.ids``)."""
+        """One decode step for all traces: token ids [N] (int32, device) in, the next
+        ids [N] out (a device tensor, also kept in ``self.ids``)."""
         if self.length >= self.cfg.max_len:
             raise ValueError("KV cache is full")
         self._enqueue(ids, device_lengths=False)
@@ -146,6 +222,7 @@ class Int4Decoder:
         so the graph replays unchanged while the cache grows. Run one eager step first
         (plans and tensor maps are cached on the first call of each shape)."""
         t = _lib.torch()
+        self._ensure_exchange()
         g = t.cuda.CUDAGraph()
         side = t.cuda.Stream(device=self.dev)
         side.wait_stream(t.cuda.current_stream(self.dev))
@@ -164,17 +241,51 @@ class Int4Decoder:
         self.length += 1
         return self.ids
 
+    def _ensure_exchange(self):
+        """Map the other ranks' exchange buffers (a collective: every rank's first step
+        or capture makes it)."""
+        if self.world > 1 and self.exchange == "peer" and self.peer is None:
+            from .peer import PeerExchange
+            self.peer = PeerExchange(self.N, self.cfg.hidden, self.dev, group=self.group,
+                                     timeout_s=self.exchange_timeout_s)
+
+    def close(self):
+        """Release the captured graph and the exchange buffers (before the process group
+        is destroyed)."""
+        t = _lib.torch()
+        self.graph = None
+        t.cuda.synchronize(self.dev)
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
+    def _residual_norm(self, y, w, st):
+        """x += y (the sum over ranks of the row-parallel partials y), h = RMSNorm(x) * w."""
+        cfg, N, L = self.cfg, self.N, lib()
+        p = lambda x: x.data_ptr()  # noqa: E731
+        if y is not None and self.world > 1:
+            if self.exchange == "peer":
+                self.peer.add_rmsnorm(y, self.x, w, cfg.eps, self.h, self.err, st)
+                return
+            import torch.distributed as dist
+            dist.all_reduce(y, group=self.group)
+        check(L.mb_add_rmsnorm(p(self.x), None if y is None else p(y), p(w), N, cfg.hidden, cfg.eps, p(self.h), st),
+              "mb_add_rmsnorm")
+
     def _enqueue(self, ids, device_lengths: bool):
         cfg, N, L = self.cfg, self.N, lib()
-        D, H, dh, F, V = cfg.hidden, cfg.heads, cfg.head_dim, cfg.ffn, cfg.vocab
+        D, dh = cfg.hidden, cfg.head_dim
+        H, F, V = self.Hl, self.Fl, self.Vl  # this rank's heads, FFN columns, vocabulary columns
+        Dl = H * dh
+        self._ensure_exchange()
         st = stream_of(self.dev)
         p = lambda x: x.data_ptr()  # noqa: E731
         err = p(self.err)
-        check(L.mb_embed(p(ids), N, p(self.embed), V, D, p(self.x), err, st), "mb_embed")
+        check(L.mb_embed(p(ids), N, p(self.embed), cfg.vocab, D, p(self.x), err, st), "mb_embed")
         y = None
         for li, lw in enumerate(self.layers):
-            check(L.mb_add_rmsnorm(p(self.x), y, p(lw["attn_norm"]), N, D, cfg.eps, p(self.h), st), "mb_add_rmsnorm")
-            check(L.mb_int4_gemm(p(self.h), p(lw["wqkv"]), p(self.qkv), N, D, 3 * D, err, st), "qkv")
+            self._residual_norm(y, lw["attn_norm"], st)
+            check(L.mb_int4_gemm(p(self.h), p(lw["wqkv"]), p(self.qkv), N, D, 3 * Dl, err, st), "qkv")
             check(L.mb_rope_append(p(self.qkv), N, H, dh, p(self.pos), p(self.cs), cfg.max_len, p(self.q),
                                    p(self.k_cache[li]), p(self.v_cache[li]), err, st), "mb_rope_append")
             if device_lengths:  # length = position + 1, read on the device
@@ -187,20 +298,30 @@ class Int4Decoder:
                                              self.length + 1, cfg.max_len, dh, self.scale, p(self.table),
                                              self.lut.size, float(self.lut.range_max), p(self.ws), self.ws.numel(),
                                              st), "mb_decode_attn_cache")
-            check(L.mb_int4_gemm(p(self.att), p(lw["wo"]), p(self.o), N, D, D, err, st), "o_proj")
-            check(L.mb_add_rmsnorm(p(self.x), p(self.o), p(lw["ffn_norm"]), N, D, cfg.eps, p(self.h), st),
-                  "mb_add_rmsnorm")
+            check(L.mb_int4_gemm(p(self.att), p(lw["wo"]), p(self.o), N, Dl, D, err, st), "o_proj")
+            self._residual_norm(self.o, lw["ffn_norm"], st)  # row-parallel o_proj joined over ranks
             check(L.mb_int4_gemm(p(self.h), p(lw["wgu"]), p(self.gu), N, D, 2 * F, err, st), "gate_up")
             check(L.mb_swiglu(p(self.gu), N, F, p(self.a), st), "mb_swiglu")
             check(L.mb_int4_gemm(p(self.a), p(lw["wd"]), p(self.o), N, F, D, err, st), "down")
-            y = p(self.o)
-        check(L.mb_add_rmsnorm(p(self.x), y, p(self.final_norm), N, D, cfg.eps, p(self.h), st), "final norm")
+            y = self.o  # row-parallel down projection, joined by the next norm
+        self._residual_norm(y, self.final_norm, st)
         check(L.mb_int4_gemm(p(self.h), p(self.lm_head), p(self.logits), N, D, V, err, st), "lm_head")
-        check(L.mb_argmax_f16(p(self.logits), N, V, p(self.ids), st), "mb_argmax_f16")
+        if self.sampler is not None:
+            self.sampler.sample(self.logits, self.temperature, tokens=self.ids, logprobs=self.logprobs, err=self.err,
+                                stream=st)
+        elif self.world == 1:
+            check(L.mb_argmax_f16(p(self.logits), N, V, p(self.ids), st), "mb_argmax_f16")
+        elif self.exchange == "peer":  # per-shard keys exchanged over NVLink, max -> ids, one kernel
+            self.peer.argmax(self.logits, self.v0, self.ids, self.err, st)
+        else:  # per-shard keys, one int64 MAX all-reduce, keys -> ids
+            import torch.distributed as dist
+            check(L.mb_argmax_key_f16(p(self.logits), N, V, self.v0, p(self.keys), st), "mb_argmax_key_f16")
+            dist.all_reduce(self.keys, op=dist.ReduceOp.MAX, group=self.group)
+            check(L.mb_argmax_keys_to_ids(p(self.keys), N, p(self.ids), st), "mb_argmax_keys_to_ids")
         check(L.mb_advance_positions(p(self.pos), N, st), "mb_advance_positions")
 
     def generate(self, first_ids, steps: int):
-        """Greedy decode ``steps`` tokens from ``first_ids`` [N]; returns [steps, N] ids
+        """Decode ``steps`` tokens from ``first_ids`` [N]; returns [steps, N] ids
         (device, int32)."""
         t = _lib.torch()
         out = t.empty((steps, self.N), dtype=t.int32, device=self.dev)
@@ -211,16 +332,51 @@ class Int4Decoder:
         return out
 
 
-__all__ = ["DecoderConfig", "Int4Decoder", "rope_table"]
+def timed_decode(dec: Int4Decoder, steps: int, warmup: int = 3, graph: bool = True) -> float:
+    """Milliseconds per decode step, CUDA-event timed on this rank after ``warmup``
+    steps (one eager step first, which caches the GEMM plans and tensor maps, then the
+    step captured as a CUDA graph unless ``graph`` is False); the maximum over ranks
+    when the decoder is tensor-parallel."""
+    t = _lib.torch()
+    dec.step(dec.ids)
+    if graph:
+        dec.capture()
+    step = dec.step_graphed if graph else (lambda: dec.step(dec.ids))
+    for _ in range(warmup):
+        step()
+    t.cuda.synchronize()
+    if dec.world > 1:
+        import torch.distributed as dist
+        dist.barrier(group=dec.group)
+        t.cuda.synchronize()
+    e0, e1 = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    t.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if dec.world > 1:
+        import torch.distributed as dist
+        m = t.tensor([ms], dtype=t.float64, device=dec.dev)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX, group=dec.group)
+        ms = float(m.item())
+    return ms
+
+
+__all__ = ["DecoderConfig", "Int4Decoder", "rope_table", "timed_decode", "tp_shards"]
 
 
 def main(argv=None) -> int:
     """``python -m moat_b200.decode``: build the config-5 decoder (random INT4 weights),
-    seed a prompt-length KV cache and time greedy decode steps (CUDA graph replay by
-    default, ``--eager`` for per-kernel launches)."""
+    seed a prompt-length KV cache and time decode steps (CUDA graph replay by default,
+    ``--eager`` for per-kernel launches). Under ``torchrun`` with N processes the
+    decoder is tensor-parallel over N GPUs (the joins inside the graph)."""
     import argparse
     import json
+    import os
     import time
+    from datetime import timedelta
     ap = argparse.ArgumentParser(description=main.__doc__)
     ap.add_argument("--traces", type=int, default=16)
     ap.add_argument("--prompt", type=int, default=512)
@@ -228,32 +384,39 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--eager", action="store_true")
+    ap.add_argument("--temperature", type=float, default=0.0, help="> 0: top-50 sampling (one GPU)")
+    ap.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
+                    help="how tensor-parallel ranks join their partial products (N > 1)")
     args = ap.parse_args(argv)
     t = _lib.require_cuda()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dev = t.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    t.cuda.set_device(dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     cfg = DecoderConfig(layers=args.layers, max_len=max(768, args.prompt + args.warmup + args.steps + 2))
     t0 = time.perf_counter()
-    dec = Int4Decoder(cfg, args.traces, seed=0)
-    dec.fill_prompt_cache(args.prompt, seed=1)
-    dec.ids.copy_(t.arange(args.traces, dtype=t.int32, device=dec.dev) * 7919 % cfg.vocab)
-    dec.step(dec.ids)
-    if not args.eager:
-        dec.capture()
-    step = (lambda: dec.step(dec.ids)) if args.eager else dec.step_graphed
-    for _ in range(args.warmup):
-        step()
-    t.cuda.synchronize()
-    build = time.perf_counter() - t0
-    e0, e1 = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        step()
-    e1.record()
-    t.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    print(json.dumps({"tok_per_s": args.traces / ms * 1e3, "ms_per_step": ms, "traces": args.traces,
-                      "layers": cfg.layers, "prompt": args.prompt, "steps": args.steps,
-                      "mode": "eager" if args.eager else "graph", "setup_s": build,
-                      "device_error_bits": int(dec.err.item())}))
+    dec = Int4Decoder(cfg, args.traces, device=dev, seed=0, rank=rank, world=world, exchange=args.exchange,
+                      temperature=args.temperature)
+    try:
+        dec.fill_prompt_cache(args.prompt, seed=1)
+        dec.ids.copy_(t.arange(args.traces, dtype=t.int32, device=dec.dev) * 7919 % cfg.vocab)
+        t.cuda.synchronize()
+        build = time.perf_counter() - t0
+        ms = timed_decode(dec, args.steps, args.warmup, graph=not args.eager)
+        if rank == 0:
+            print(json.dumps({"tok_per_s": args.traces / ms * 1e3, "ms_per_step": ms, "traces": args.traces,
+                              "layers": cfg.layers, "prompt": args.prompt, "steps": args.steps, "tp": world,
+                              "exchange": args.exchange if world > 1 else None, "temperature": args.temperature,
+                              "mode": "eager" if args.eager else "graph", "setup_s": build,
+                              "device_error_bits": int(dec.err.item())}))
+    finally:
+        dec.close()  # graph and exchange buffers go before the process group
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
     return 0
 
 

@@ -108,3 +108,42 @@ def test_host_side_argument_validation(L):
     assert L.mb_decode_attn(fake, fake, fake, fake, 1, 1, 16, 128, 1.0, fake, 32768, 16.0, fake, 16, None) == -3
     # misaligned -> MB_ERR_ALIGN (-5)
     assert L.mb_int4_dequant(ctypes.c_void_p(0x10001), fake, 1, None) == -5
+
+
+def test_tensor_parallel_and_sampling_entries_validate_on_the_host(L):
+    fake = ctypes.c_void_p(0x10000)
+    bufs = (ctypes.c_void_p * 2)(0x10000, 0x20000)
+    assert L.mb_peer_buffer_bytes(16, 2048) == 16384 + 2 * 8 * 16 * 2048 * 2
+    assert L.mb_peer_buffer_bytes(0, 2048) == 0 and L.mb_peer_buffer_bytes(65, 2048) == 0
+    assert L.mb_peer_buffer_bytes(16, 100) == 0
+    assert L.mb_argmax_key_f16(None, 2, 10, 0, fake, None) == -1
+    assert L.mb_argmax_key_f16(fake, 2, 10, -1, fake, None) == -2
+    assert L.mb_argmax_keys_to_ids(fake, 0, fake, None) == -2
+    assert L.mb_ipc_alloc(1024, None, fake) == -1
+    assert L.mb_ipc_open(None, fake) == -1
+    # peer exchange: null pointers, too many rows, rows larger than a slot, bad rank / world
+    assert L.mb_peer_add_rmsnorm(bufs, 2, 0, 4096, 10**9, None, fake, fake, 2, 2048, 1e-6, fake, fake, None,
+                                 None) == -1
+    assert L.mb_peer_add_rmsnorm(bufs, 2, 0, 65 * 2048, 10**9, fake, fake, fake, 65, 2048, 1e-6, fake, fake, None,
+                                 None) == -2
+    assert L.mb_peer_add_rmsnorm(bufs, 2, 0, 2048, 10**9, fake, fake, fake, 2, 2048, 1e-6, fake, fake, None,
+                                 None) == -2
+    assert L.mb_peer_add_rmsnorm(bufs, 2, 2, 4096, 10**9, fake, fake, fake, 2, 2048, 1e-6, fake, fake, None,
+                                 None) == -2
+    assert L.mb_peer_add_rmsnorm(bufs, 9, 0, 4096, 10**9, fake, fake, fake, 2, 2048, 1e-6, fake, fake, None,
+                                 None) == -2
+    assert L.mb_peer_argmax(bufs, 2, 0, 4096, 0, fake, 2, 10, 0, fake, fake, None, None) == -2   # no timeout
+    assert L.mb_peer_argmax(bufs, 2, 0, 4096, 10**9, fake, 2, 10, 0, None, fake, None, None) == -1
+    # sampler: sizes, workspace, top_k range, dtype flag
+    assert L.mb_sample_workspace_size(16, 151936) == (16 * 151936 * 2 + 255) // 256 * 256
+    assert L.mb_sample_workspace_size(0, 10) == 0
+    args = dict(T=0.7, k=50, size=32768, r=10.0)
+
+    def samp(logits=fake, f32=0, N=2, V=100, k=50, ws_bytes=1 << 20, tokens=fake):
+        return L.mb_sample_tokens(logits, f32, N, V, args["T"], k, fake, args["size"], args["r"], None, 0, fake,
+                                  tokens, fake, fake, ws_bytes, None, None)
+    assert samp(logits=None) == -1
+    assert samp(tokens=None) == -1
+    assert samp(k=0) == -2 and samp(k=65) == -2
+    assert samp(f32=2) == -2
+    assert samp(ws_bytes=16) == -3

@@ -231,3 +231,28 @@ def test_captured_step_matches_eager_steps(cuda):
         assert eb.cpu().tolist() == ea.cpu().tolist()
     assert a.pos.cpu().tolist() == b.pos.cpu().tolist() == [262] * N
     assert int(b.err.item()) == 0
+
+
+def test_sampled_decode_step_matches_oracle_draw(cuda):
+    """temperature > 0: the step's token is the oracle's draw from the step's own
+    logits with the device stream's uniforms (counter = step), eager and replayed."""
+    import torch
+    from moat_b200.decode import DecoderConfig, Int4Decoder
+    from oracle import sampling as S
+    cfg = DecoderConfig(layers=2, hidden=256, heads=2, head_dim=128, ffn=512, vocab=1000, max_len=64)
+    N = 4
+    dec = Int4Decoder(cfg, N, device=cuda, seed=3, temperature=0.8, sample_seed=17)
+    dec.fill_prompt_cache(10, seed=4)
+    table = OA.exp_table(32768, 10.0)
+    dec.ids.copy_(torch.tensor([1, 2, 3, 4], dtype=torch.int32, device=cuda))
+    dec.step(dec.ids)
+    for c in range(4):
+        if c == 1:
+            dec.capture()
+        if c >= 1:
+            dec.step_graphed()
+        torch.cuda.synchronize()
+        otok, olp = S.sample_tokens(dec.logits.cpu().numpy(), 0.8, table, 10.0, S.uniforms(17, c, N))
+        assert dec.ids.cpu().numpy().tolist() == otok.tolist()
+        np.testing.assert_allclose(dec.logprobs.cpu().numpy(), olp, rtol=1e-6, atol=1e-6)
+    assert int(dec.err.item()) == 0
