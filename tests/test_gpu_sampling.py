@@ -81,6 +81,7 @@ def test_temperature_matches_oracle(cuda, dtype, T):
 def test_big_vocabulary_and_ties(cuda):
     x = S.make_logits(4, 151936, 11, 3.0, np.float16)
     x[1] = 0.0                     # every column ties: the first 50 columns are the set
+    x[2] = -5.0
     x[2, :64] = 5.0                # 64 ties at the top: the first 50 of them
     u = np.array([0.1, 0.999, 0.5, 0.0], np.float32)
     tok, lp, err = _run(x, 0.7, cuda, uniforms=u)
