@@ -344,6 +344,7 @@ def run_moat(args):
 
     attn = None if (world > 1 or args.no_attn) else attention_side(dev, peak, peak_kind, with_cpu=not args.no_cpu)
     decode = None if args.no_decode else decode_side(dev, rank, world)
+    sampling = None if (world > 1 or args.no_decode) else sampling_side(dev)
 
     if rank == 0:
         cpu = None if (world > 1 or args.no_cpu) else cpu_reference(budget_s=args.cpu_seconds)
@@ -370,6 +371,7 @@ def run_moat(args):
             "cpu_baseline": cpu,
             "attention": attn,
             "decode": decode,
+            "sampling": sampling,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -490,6 +492,31 @@ def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 64):
             "exchange": "NVLink peer stores (mb_peer_add_rmsnorm, mb_peer_argmax)" if world > 1 else None,
             "bytes_per_step": step_bytes, "GBps": step_bytes / ms / 1e6, "device_error_bits": err,
             "data": "synthetic (random-init weights quantized to INT4; KV cache seeded N(0,1))"}
+
+
+def sampling_side(dev, calls: int = 50):
+    """Batched sampler speed on the config-5 LM-head output shape: 16 rows of 151936
+    fp16 logits, temperature 0.7, top-50 of the LUT softmax (``mb_sample_tokens``),
+    CUDA-event timed over back-to-back calls after warm-up."""
+    import torch
+    from moat_b200.sampling import BatchSampler
+    N, V = 16, 151936
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 9)
+    logits = (torch.randn((N, V), generator=g, device=dev) * 3.0).half()
+    s = BatchSampler(N, V, device=dev, seed=SEED)
+    for _ in range(5):
+        s.sample(logits, 0.7)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(calls):
+        s.sample(logits, 0.7)
+    e1.record()
+    torch.cuda.synchronize()
+    return {"workload": "mb_sample_tokens: 16 x 151936 fp16 logits, T=0.7, top-50, LUT range 10",
+            "us_per_call": e0.elapsed_time(e1) / calls * 1e3, "calls": calls,
+            "device_error_bits": int(s.err.item())}
 
 
 def run_e2e(args, dev, stream, shard, sweep, Ms, world, rank, bounds, R):

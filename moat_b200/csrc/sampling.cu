@@ -17,7 +17,9 @@
 // makes the reference raise; here it sets MB_DEVERR_NONFINITE, token = the argmax,
 // logprob = NaN.
 //
-// One CTA of 1024 threads per row:
+// One cluster of C <= 8 CTAs (1024 threads each) per row, CTA r owning a contiguous
+// column range; row-wide sums, maxima and histograms are joined through distributed
+// shared memory:
 //   A  max and first argmax of the raw logits (the scaled maximum is the scaled value
 //      at that column: the scaling is monotone);
 //   B  per element the table index of (s - max) into a uint16 scratch row, and the
@@ -27,9 +29,13 @@
 //   C, D  256-bin histograms of the high, then the low byte of the fp16 probability
 //      bits give the k-th largest probability t;
 //   E  every column with p > t, and the first (k - #{p > t}) columns with p == t in
-//      column order (per-thread contiguous ranges and a block prefix sum);
-//   a warp ranks the <= 64 candidate keys (p << 32 | ~column), thread 0 draws.
+//      column order (per-thread contiguous ranges, a block prefix sum, and the tie
+//      counts of the lower-ranked CTAs);
+//   the leader CTA gathers the <= 64 candidate keys (p << 32 | ~column), a warp ranks
+//   them, thread 0 draws.
 #include <cuda_fp16.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 
@@ -132,53 +138,105 @@ __device__ __forceinline__ int pick_bin(const uint32_t* hist, uint32_t need, uin
   return 0;
 }
 
-__global__ void __launch_bounds__(kSampBlock) k_sample(SampArgs a) {
+__device__ __forceinline__ unsigned long long ld_cluster_u64(const void* local, uint32_t rank) {
+  unsigned long long v;
+  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(mapa_shared(smem_u32(local), rank)) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_cluster_u32(const void* local, uint32_t rank) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(mapa_shared(smem_u32(local), rank)) : "memory");
+  return v;
+}
+
+// One cluster of gridDim.x CTAs per row (blockIdx.y); CTA r of the cluster owns the
+// contiguous columns [r * chunk, (r + 1) * chunk). Row-wide values are reduced through
+// distributed shared memory: each CTA publishes its partial in its own shared memory,
+// a cluster barrier, then every CTA (or the leader, rank 0) reads the partials of all
+// ranks in rank order. Every CTA of a cluster takes the same branches (they derive
+// from row-wide values), so all pass the same cluster barriers.
+__global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
   extern __shared__ uint16_t ptab[];  // [size] fp16 probability bits per table index
   __shared__ unsigned long long red[kSampBlock / 32];
-  __shared__ uint32_t hist[256];
+  __shared__ unsigned long long part_a, part_b, bcast;
+  __shared__ uint32_t hist_c[256], hist_d[256], gh[256];
   __shared__ uint32_t scan[kSampBlock / 32];
-  __shared__ unsigned long long cand[kSampMaxK];
-  __shared__ unsigned long long sorted[kSampMaxK];
-  __shared__ uint32_t ncand;
+  __shared__ unsigned long long lc[kSampMaxK], lt[kSampMaxK], cand[kSampMaxK], sorted[kSampMaxK];
+  __shared__ uint32_t lcn, ltn, lties;
   __shared__ uint32_t sel[4];  // bin, above, threshold, c_gt
   pdl_wait();
   pdl_launch_dependents();
-  const int n = blockIdx.x;
+  const int C = static_cast<int>(gridDim.x);
+  const uint32_t r = cluster_ctarank();
+  const int n = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t row = static_cast<int64_t>(n) * a.V;
   uint16_t* srow = a.scratch + row;
+  const int chunk = (a.V + C - 1) / C;
+  const int cb = min(a.V, static_cast<int>(r) * chunk), ce = min(a.V, cb + chunk);
+  if (tid == 0) {
+    lcn = 0;
+    ltn = 0;
+    lties = 0;
+  }
+  for (int b = tid; b < 256; b += kSampBlock) {
+    hist_c[b] = 0;
+    hist_d[b] = 0;
+  }
 
-  // A: first index of the largest raw logit (NaN largest)
+  // A: first index of the largest raw logit (NaN largest), row-wide
   unsigned long long best = 0;
-  for (int c = tid; c < a.V; c += kSampBlock) {
+  for (int c = cb + tid; c < ce; c += kSampBlock) {
     const unsigned long long key =
         (static_cast<unsigned long long>(samp_code(samp_raw(a, row + c))) << 32) | (0xFFFFFFFFull - c);
     best = key > best ? key : best;
   }
   best = block_max_u64(best, red);
+  if (tid == 0) part_a = best;
+  cluster_sync();
+  if (tid == 0) {
+    unsigned long long b = 0;
+    for (int q = 0; q < C; ++q) {
+      const unsigned long long v = ld_cluster_u64(&part_a, q);
+      b = v > b ? v : b;
+    }
+    bcast = b;
+  }
+  __syncthreads();
+  best = bcast;
   const int amax = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
   const float m = samp_scaled(a, samp_raw(a, row + amax));
   const uint32_t counter = *reinterpret_cast<volatile uint32_t*>(a.rng_state);
+  const bool leader = r == 0;
   if (!isfinite(m)) {  // the reference raises on a non-finite maximum
-    if (tid == 0) {
+    if (leader && tid == 0) {
       if (a.err) atomicOr(a.err, MB_DEVERR_NONFINITE);
       a.tokens[n] = amax;
       a.logprobs[n] = __int_as_float(0x7fc00000);
     }
   } else {
-    // B: table indices and the exact sum of the table values
+    // B: table indices and the exact sum of the table values, row-wide
     unsigned long long acc = 0;
-    for (int c = tid; c < a.V; c += kSampBlock) {
+    for (int c = cb + tid; c < ce; c += kSampBlock) {
       const int j = samp_lut_index(samp_scaled(a, samp_raw(a, row + c)) - m, a.step, a.size);
       if (a.scale) srow[c] = static_cast<uint16_t>(j);
       const float e = __half2float(__ushort_as_half(__ldg(a.table + (a.size - 1 - j))));
       acc += static_cast<unsigned long long>(e * 16777216.0f);  // exact: e is a multiple of 2^-24, <= 1
     }
     acc = block_sum_u64(acc, red);
-    float sum = __ull2float_rn(acc) * 5.9604644775390625e-8f;  // * 2^-24, exact
+    if (tid == 0) part_b = acc;
+    cluster_sync();
+    if (tid == 0) {
+      unsigned long long t = 0;
+      for (int q = 0; q < C; ++q) t += ld_cluster_u64(&part_b, q);
+      bcast = t;
+    }
+    __syncthreads();
+    float sum = __ull2float_rn(bcast) * 5.9604644775390625e-8f;  // * 2^-24, exact
     if (!(sum > 0.0f)) sum = 1.0f;
     if (!a.scale) {
-      if (tid == 0) {
+      if (leader && tid == 0) {
         const float e0 = __half2float(__ushort_as_half(__ldg(a.table + (a.size - 1))));
         const float p = __half2float(__float2half_rn(__fdiv_rn(e0, sum)));
         a.tokens[n] = amax;
@@ -190,57 +248,67 @@ __global__ void __launch_bounds__(kSampBlock) k_sample(SampArgs a) {
         const float e = __half2float(__ushort_as_half(__ldg(a.table + (a.size - 1 - j))));
         ptab[j] = __half_as_ushort(__float2half_rn(__fdiv_rn(e, sum)));
       }
-      for (int b = tid; b < 256; b += kSampBlock) hist[b] = 0;
       __syncthreads();
       const uint32_t k = static_cast<uint32_t>(a.k);
-      // C: high byte histogram
-      for (int base = 0; base < a.V; base += kSampBlock) {
+      // C: high byte histogram, row-wide
+      for (int base = cb; base < ce; base += kSampBlock) {
         const int c = base + tid;
-        const int bin = c < a.V ? (ptab[__ldcg(srow + c)] >> 8) : -1;
+        const int bin = c < ce ? (ptab[__ldcg(srow + c)] >> 8) : -1;
         const unsigned peers = __match_any_sync(0xffffffffu, bin);
-        if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+        if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist_c[bin], static_cast<uint32_t>(__popc(peers)));
+      }
+      __syncthreads();
+      cluster_sync();
+      if (tid < 256) {
+        uint32_t t = 0;
+        for (int q = 0; q < C; ++q) t += ld_cluster_u32(&hist_c[tid], q);
+        gh[tid] = t;
       }
       __syncthreads();
       if (tid == 0) {
         uint32_t above;
-        sel[0] = static_cast<uint32_t>(pick_bin(hist, k, &above));
+        sel[0] = static_cast<uint32_t>(pick_bin(gh, k, &above));
         sel[1] = above;
       }
       __syncthreads();
       const uint32_t hb = sel[0], above_hi = sel[1];
-      for (int b = tid; b < 256; b += kSampBlock) hist[b] = 0;
-      __syncthreads();
-      // D: low byte histogram inside the high bin
-      for (int base = 0; base < a.V; base += kSampBlock) {
+      // D: low byte histogram inside the high bin, row-wide
+      for (int base = cb; base < ce; base += kSampBlock) {
         const int c = base + tid;
         int bin = -1;
-        if (c < a.V) {
+        if (c < ce) {
           const uint32_t p = ptab[__ldcg(srow + c)];
           if ((p >> 8) == hb) bin = static_cast<int>(p & 0xFFu);
         }
         const unsigned peers = __match_any_sync(0xffffffffu, bin);
-        if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+        if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist_d[bin], static_cast<uint32_t>(__popc(peers)));
+      }
+      __syncthreads();
+      cluster_sync();
+      if (tid < 256) {
+        uint32_t t = 0;
+        for (int q = 0; q < C; ++q) t += ld_cluster_u32(&hist_d[tid], q);
+        gh[tid] = t;
       }
       __syncthreads();
       if (tid == 0) {
         uint32_t above;
-        const int lo = pick_bin(hist, k - above_hi, &above);
+        const int lo = pick_bin(gh, k - above_hi, &above);
         sel[2] = (hb << 8) | static_cast<uint32_t>(lo);
         sel[3] = above_hi + above;
-        ncand = 0;
       }
       __syncthreads();
       const uint32_t t = sel[2], c_gt = sel[3];
       const uint32_t need = k - c_gt;  // >= 1 columns with p == t, the first ones by column
-      // E: contiguous column range per thread, in column order
-      const int chunk = (a.V + kSampBlock - 1) / kSampBlock;
-      const int c0 = min(a.V, tid * chunk), c1 = min(a.V, c0 + chunk);
+      // E: contiguous column range per thread inside this CTA's range, in column order
+      const int sub = (ce - cb + kSampBlock - 1) / kSampBlock;
+      const int c0 = min(ce, cb + tid * sub), c1 = min(ce, c0 + sub);
       uint32_t ties = 0;
       for (int c = c0; c < c1; ++c) {
         const uint32_t p = ptab[__ldcg(srow + c)];
         if (p > t) {
-          const uint32_t slot = atomicAdd(&ncand, 1u);
-          if (slot < kSampMaxK) cand[slot] = (static_cast<unsigned long long>(p) << 32) | (0xFFFFFFFFull - c);
+          const uint32_t slot = atomicAdd(&lcn, 1u);
+          if (slot < kSampMaxK) lc[slot] = (static_cast<unsigned long long>(p) << 32) | (0xFFFFFFFFull - c);
         } else if (p == t) {
           ++ties;
         }
@@ -263,66 +331,92 @@ __global__ void __launch_bounds__(kSampBlock) k_sample(SampArgs a) {
           if (lane >= o) s2 += x;
         }
         scan[tid] = s2 - v;  // exclusive over warps
+        if (tid == 31) lties = s2;  // this CTA's tie count
       }
       __syncthreads();
-      uint32_t rank = scan[tid >> 5] + incl - ties;
-      for (int c = c0; c < c1 && rank < need; ++c) {
+      cluster_sync();  // tie counts of every rank published
+      if (tid == 0) {
+        uint32_t off = 0;
+        for (uint32_t q = 0; q < r; ++q) off += ld_cluster_u32(&lties, q);
+        sel[0] = off;  // ties in lower ranks' columns
+        ltn = off >= need ? 0u : min(lties, need - off);
+      }
+      __syncthreads();
+      const uint32_t lim = ltn;
+      uint32_t rank = scan[tid >> 5] + incl - ties;  // local rank among this CTA's ties
+      for (int c = c0; c < c1 && rank < lim; ++c) {
         if (ptab[__ldcg(srow + c)] == t) {
-          const uint32_t slot = c_gt + rank;
-          if (slot < kSampMaxK) cand[slot] = (static_cast<unsigned long long>(t) << 32) | (0xFFFFFFFFull - c);
+          lt[rank] = (static_cast<unsigned long long>(t) << 32) | (0xFFFFFFFFull - c);
           ++rank;
         }
       }
       __syncthreads();
-      // rank the k candidate keys (distinct: the column is part of the key)
-      if (tid < 32) {
-        for (uint32_t i = tid; i < k; i += 32) {
-          const unsigned long long key = cand[i];
-          uint32_t r = 0;
-          for (uint32_t j = 0; j < k; ++j) r += cand[j] > key ? 1u : 0u;
-          sorted[r] = key;
-        }
-      }
-      __syncthreads();
-      if (tid == 0) {
-        float u;
-        if (a.uniforms) {
-          u = a.uniforms[n];
-        } else {
-          const unsigned long long base =
-              splitmix64(a.seed ^ (static_cast<unsigned long long>(counter) * 0xD1B54A32D192ED03ull));
-          u = static_cast<float>(splitmix64(base + static_cast<unsigned long long>(n)) >> 40) *
-              5.9604644775390625e-8f;
-        }
-        float total = 0.0f;
-        for (uint32_t i = 0; i < k; ++i)
-          total += __half2float(__ushort_as_half(static_cast<uint16_t>(sorted[i] >> 32)));
-        uint32_t pick = k - 1;
-        if (total > 0.0f) {
-          const float target = u * total;
-          float run = 0.0f;
-          for (uint32_t i = 0; i < k; ++i) {
-            run += __half2float(__ushort_as_half(static_cast<uint16_t>(sorted[i] >> 32)));
-            if (run > target) {
-              pick = i;
-              break;
-            }
+      cluster_sync();  // candidate lists of every rank published
+      if (leader) {
+        if (tid == 0) {
+          uint32_t pos = 0;
+          for (int q = 0; q < C; ++q) {
+            const uint32_t n1 = min(ld_cluster_u32(&lcn, q), static_cast<uint32_t>(kSampMaxK));
+            for (uint32_t i = 0; i < n1 && pos < k; ++i) cand[pos++] = ld_cluster_u64(&lc[i], q);
           }
-        } else {
-          pick = min(static_cast<uint32_t>(floorf(u * static_cast<float>(k))), k - 1);
+          for (int q = 0; q < C; ++q) {
+            const uint32_t n2 = ld_cluster_u32(&ltn, q);
+            for (uint32_t i = 0; i < n2 && pos < k; ++i) cand[pos++] = ld_cluster_u64(&lt[i], q);
+          }
+          for (; pos < k; ++pos) cand[pos] = 0;  // unreachable when the counts agree
         }
-        const unsigned long long key = sorted[pick];
-        const float p = __half2float(__ushort_as_half(static_cast<uint16_t>(key >> 32)));
-        a.tokens[n] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
-        a.logprobs[n] = logf(fmaxf(p, 1e-10f));
+        __syncthreads();
+        // rank the k candidate keys (distinct: the column is part of the key)
+        if (tid < 32) {
+          for (uint32_t i = tid; i < k; i += 32) {
+            const unsigned long long key = cand[i];
+            uint32_t rk = 0;
+            for (uint32_t j = 0; j < k; ++j) rk += cand[j] > key ? 1u : 0u;
+            sorted[rk] = key;
+          }
+        }
+        __syncthreads();
+        if (tid == 0) {
+          float u;
+          if (a.uniforms) {
+            u = a.uniforms[n];
+          } else {
+            const unsigned long long base =
+                splitmix64(a.seed ^ (static_cast<unsigned long long>(counter) * 0xD1B54A32D192ED03ull));
+            u = static_cast<float>(splitmix64(base + static_cast<unsigned long long>(n)) >> 40) *
+                5.9604644775390625e-8f;
+          }
+          float total = 0.0f;
+          for (uint32_t i = 0; i < k; ++i)
+            total += __half2float(__ushort_as_half(static_cast<uint16_t>(sorted[i] >> 32)));
+          uint32_t pick = k - 1;
+          if (total > 0.0f) {
+            const float target = u * total;
+            float run = 0.0f;
+            for (uint32_t i = 0; i < k; ++i) {
+              run += __half2float(__ushort_as_half(static_cast<uint16_t>(sorted[i] >> 32)));
+              if (run > target) {
+                pick = i;
+                break;
+              }
+            }
+          } else {
+            pick = min(static_cast<uint32_t>(floorf(u * static_cast<float>(k))), k - 1);
+          }
+          const unsigned long long key = sorted[pick];
+          const float p = __half2float(__ushort_as_half(static_cast<uint16_t>(key >> 32)));
+          a.tokens[n] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
+          a.logprobs[n] = logf(fmaxf(p, 1e-10f));
+        }
       }
     }
   }
-  // the last CTA advances the random stream's counter (read by the next call)
-  __syncthreads();
-  if (tid == 0) {
+  // no CTA leaves while the leader may still read its shared memory
+  cluster_sync();
+  // the last row's leader advances the random stream's counter (read by the next call)
+  if (leader && tid == 0) {
     __threadfence();
-    if (atomicAdd(a.rng_state + 1, 1u) == gridDim.x - 1) {
+    if (atomicAdd(a.rng_state + 1, 1u) == gridDim.y - 1) {
       a.rng_state[1] = 0;
       a.rng_state[0] = counter + 1;
       __threadfence();
@@ -373,7 +467,30 @@ int32_t mb_sample_tokens(const void* logits, int32_t logits_f32, int32_t N, int3
       cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
           cudaSuccess)
     return MB_ERR_LAUNCH;
-  return launch_with_pdl(k_sample, dim3(N), dim3(kSampBlock), smem, static_cast<cudaStream_t>(stream), a);
+  // cluster size: up to 8 CTAs per row while the rows' clusters fit the GPU at once
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  (void)cudaGetLastError();
+  const int C = std::max(1, std::min(8, sms / N));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C, N);
+  cfg.blockDim = dim3(kSampBlock);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = C;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (cudaLaunchKernelEx(&cfg, k_sample, a) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return MB_ERR_LAUNCH;
+  }
+  return launch_status();
 }
 
 }  // extern "C"
