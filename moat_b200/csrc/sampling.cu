@@ -36,6 +36,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -123,19 +124,43 @@ __device__ __forceinline__ uint32_t samp_code(float v) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-// Walks the 256 bins from the top: the bin holding the `need`-th largest element.
-// Returns the bin and writes the count of elements in higher bins.
-__device__ __forceinline__ int pick_bin(const uint32_t* hist, uint32_t need, uint32_t* above) {
-  uint32_t cum = 0;
-  for (int b = 255; b >= 0; --b) {
-    if (cum + hist[b] >= need) {
-      *above = cum;
-      return b;
-    }
-    cum += hist[b];
+// The bin holding the `need`-th largest element, walking the 256 bins from the top, by
+// one warp: lane l sums bins 255-8l .. 248-8l, a scan over the lanes
+// (highest bins first) finds the lane holding the `need`-th largest element, which walks
+// its 8 bins. All 32 lanes call it; every lane returns the bin and `above` (the count
+// of elements in higher bins).
+__device__ __forceinline__ int pick_bin_warp(const uint32_t* hist, uint32_t need, uint32_t* above) {
+  const int lane = threadIdx.x & 31;
+  uint32_t s = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s += hist[255 - 8 * lane - i];
+  uint32_t incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += x;
   }
-  *above = cum;
-  return 0;
+  const unsigned hit = __ballot_sync(0xffffffffu, incl >= need);
+  const int f = hit ? __ffs(hit) - 1 : 31;
+  int bin = 0;
+  uint32_t ab = 0;
+  if (lane == f) {
+    uint32_t cum = incl - s;
+    bin = 255 - 8 * lane - 7;
+    ab = cum;
+    for (int i = 0; i < 8; ++i) {
+      const int b = 255 - 8 * lane - i;
+      if (cum + hist[b] >= need) {
+        bin = b;
+        ab = cum;
+        break;
+      }
+      cum += hist[b];
+    }
+  }
+  bin = __shfl_sync(0xffffffffu, bin, f);
+  *above = __shfl_sync(0xffffffffu, ab, f);
+  return bin;
 }
 
 __device__ __forceinline__ unsigned long long ld_cluster_u64(const void* local, uint32_t rank) {
@@ -164,7 +189,16 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
   __shared__ uint32_t scan[kSampBlock / 32];
   __shared__ unsigned long long lc[kSampMaxK], lt[kSampMaxK], cand[kSampMaxK], sorted[kSampMaxK];
   __shared__ uint32_t lcn, ltn, lties;
+  __shared__ uint32_t gcnt[2 * 8 + 1];  // leader: per-rank candidate counts (> t, then ties) and their prefix
   __shared__ uint32_t sel[4];  // bin, above, threshold, c_gt
+  // the exp table into shared memory (it does not depend on the previous kernel, so
+  // this overlaps its tail); ptab holds table[j] until it becomes the probability table
+  if ((a.size & 7) == 0 && (reinterpret_cast<uintptr_t>(a.table) & 15) == 0) {
+    for (int j = threadIdx.x; j < a.size / 8; j += kSampBlock)
+      reinterpret_cast<uint4*>(ptab)[j] = __ldg(reinterpret_cast<const uint4*>(a.table) + j);
+  } else {
+    for (int j = threadIdx.x; j < a.size; j += kSampBlock) ptab[j] = __ldg(a.table + j);
+  }
   pdl_wait();
   pdl_launch_dependents();
   const int C = static_cast<int>(gridDim.x);
@@ -186,13 +220,24 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
   }
 
   // A: first index of the largest raw logit (NaN largest), row-wide
+  constexpr int kU = 8;  // loads issued before any is used
   unsigned long long best = 0;
-  for (int c = cb + tid; c < ce; c += kSampBlock) {
-    const unsigned long long key =
-        (static_cast<unsigned long long>(samp_code(samp_raw(a, row + c))) << 32) | (0xFFFFFFFFull - c);
-    best = key > best ? key : best;
+  for (int base = cb + tid; base < ce; base += kU * kSampBlock) {
+    float v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int c = base + u * kSampBlock;
+      v[u] = c < ce ? samp_raw(a, row + c) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int c = base + u * kSampBlock;
+      const unsigned long long key =
+          (static_cast<unsigned long long>(samp_code(v[u])) << 32) | (0xFFFFFFFFull - c);
+      if (c < ce) best = key > best ? key : best;
+    }
   }
-  best = block_max_u64(best, red);
+  best = block_max_u64(best, red);  // its barriers also publish the staged table
   if (tid == 0) part_a = best;
   cluster_sync();
   if (tid == 0) {
@@ -218,11 +263,23 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
   } else {
     // B: table indices and the exact sum of the table values, row-wide
     unsigned long long acc = 0;
-    for (int c = cb + tid; c < ce; c += kSampBlock) {
-      const int j = samp_lut_index(samp_scaled(a, samp_raw(a, row + c)) - m, a.step, a.size);
-      if (a.scale) srow[c] = static_cast<uint16_t>(j);
-      const float e = __half2float(__ushort_as_half(__ldg(a.table + (a.size - 1 - j))));
-      acc += static_cast<unsigned long long>(e * 16777216.0f);  // exact: e is a multiple of 2^-24, <= 1
+    for (int base = cb + tid; base < ce; base += kU * kSampBlock) {
+      float v[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int c = base + u * kSampBlock;
+        v[u] = c < ce ? samp_raw(a, row + c) : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int c = base + u * kSampBlock;
+        if (c < ce) {
+          const int j = samp_lut_index(samp_scaled(a, v[u]) - m, a.step, a.size);
+          if (a.scale) srow[c] = static_cast<uint16_t>(j);
+          const float e = __half2float(__ushort_as_half(ptab[a.size - 1 - j]));
+          acc += static_cast<unsigned long long>(e * 16777216.0f);  // exact: e is a multiple of 2^-24, <= 1
+        }
+      }
     }
     acc = block_sum_u64(acc, red);
     if (tid == 0) part_b = acc;
@@ -237,25 +294,36 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
     if (!(sum > 0.0f)) sum = 1.0f;
     if (!a.scale) {
       if (leader && tid == 0) {
-        const float e0 = __half2float(__ushort_as_half(__ldg(a.table + (a.size - 1))));
+        const float e0 = __half2float(__ushort_as_half(ptab[a.size - 1]));
         const float p = __half2float(__float2half_rn(__fdiv_rn(e0, sum)));
         a.tokens[n] = amax;
         a.logprobs[n] = __half2float(__float2half_rn(logf(p)));
       }
     } else {
-      // probability bits per table index
-      for (int j = tid; j < a.size; j += kSampBlock) {
-        const float e = __half2float(__ushort_as_half(__ldg(a.table + (a.size - 1 - j))));
-        ptab[j] = __half_as_ushort(__float2half_rn(__fdiv_rn(e, sum)));
+      // probability bits per table index, in place: ptab[j] = fp16(table[S-1-j] / sum)
+      // (entries j and S-1-j swap, one thread per pair)
+      for (int j = tid; j < (a.size + 1) / 2; j += kSampBlock) {
+        const int jj = a.size - 1 - j;
+        const float lo = __half2float(__ushort_as_half(ptab[j])), hi = __half2float(__ushort_as_half(ptab[jj]));
+        ptab[j] = __half_as_ushort(__float2half_rn(__fdiv_rn(hi, sum)));
+        ptab[jj] = __half_as_ushort(__float2half_rn(__fdiv_rn(lo, sum)));
       }
       __syncthreads();
       const uint32_t k = static_cast<uint32_t>(a.k);
       // C: high byte histogram, row-wide
-      for (int base = cb; base < ce; base += kSampBlock) {
-        const int c = base + tid;
-        const int bin = c < ce ? (ptab[__ldcg(srow + c)] >> 8) : -1;
-        const unsigned peers = __match_any_sync(0xffffffffu, bin);
-        if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist_c[bin], static_cast<uint32_t>(__popc(peers)));
+      for (int base = cb; base < ce; base += kU * kSampBlock) {  // trip count uniform over the warp
+        uint32_t jv[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int c = base + u * kSampBlock + tid;
+          jv[u] = c < ce ? __ldcg(srow + c) : 0xFFFFu;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int bin = jv[u] != 0xFFFFu ? (ptab[jv[u]] >> 8) : -1;
+          const unsigned peers = __match_any_sync(0xffffffffu, bin);
+          if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist_c[bin], static_cast<uint32_t>(__popc(peers)));
+        }
       }
       __syncthreads();
       cluster_sync();
@@ -265,23 +333,34 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
         gh[tid] = t;
       }
       __syncthreads();
-      if (tid == 0) {
+      if (tid < 32) {
         uint32_t above;
-        sel[0] = static_cast<uint32_t>(pick_bin(gh, k, &above));
-        sel[1] = above;
+        const int b = pick_bin_warp(gh, k, &above);
+        if (tid == 0) {
+          sel[0] = static_cast<uint32_t>(b);
+          sel[1] = above;
+        }
       }
       __syncthreads();
       const uint32_t hb = sel[0], above_hi = sel[1];
       // D: low byte histogram inside the high bin, row-wide
-      for (int base = cb; base < ce; base += kSampBlock) {
-        const int c = base + tid;
-        int bin = -1;
-        if (c < ce) {
-          const uint32_t p = ptab[__ldcg(srow + c)];
-          if ((p >> 8) == hb) bin = static_cast<int>(p & 0xFFu);
+      for (int base = cb; base < ce; base += kU * kSampBlock) {
+        uint32_t jv[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int c = base + u * kSampBlock + tid;
+          jv[u] = c < ce ? __ldcg(srow + c) : 0xFFFFu;
         }
-        const unsigned peers = __match_any_sync(0xffffffffu, bin);
-        if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist_d[bin], static_cast<uint32_t>(__popc(peers)));
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          int bin = -1;
+          if (jv[u] != 0xFFFFu) {
+            const uint32_t p = ptab[jv[u]];
+            if ((p >> 8) == hb) bin = static_cast<int>(p & 0xFFu);
+          }
+          const unsigned peers = __match_any_sync(0xffffffffu, bin);
+          if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist_d[bin], static_cast<uint32_t>(__popc(peers)));
+        }
       }
       __syncthreads();
       cluster_sync();
@@ -291,11 +370,13 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
         gh[tid] = t;
       }
       __syncthreads();
-      if (tid == 0) {
+      if (tid < 32) {
         uint32_t above;
-        const int lo = pick_bin(gh, k - above_hi, &above);
-        sel[2] = (hb << 8) | static_cast<uint32_t>(lo);
-        sel[3] = above_hi + above;
+        const int lo = pick_bin_warp(gh, k - above_hi, &above);
+        if (tid == 0) {
+          sel[2] = (hb << 8) | static_cast<uint32_t>(lo);
+          sel[3] = above_hi + above;
+        }
       }
       __syncthreads();
       const uint32_t t = sel[2], c_gt = sel[3];
@@ -304,13 +385,21 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
       const int sub = (ce - cb + kSampBlock - 1) / kSampBlock;
       const int c0 = min(ce, cb + tid * sub), c1 = min(ce, c0 + sub);
       uint32_t ties = 0;
-      for (int c = c0; c < c1; ++c) {
-        const uint32_t p = ptab[__ldcg(srow + c)];
-        if (p > t) {
-          const uint32_t slot = atomicAdd(&lcn, 1u);
-          if (slot < kSampMaxK) lc[slot] = (static_cast<unsigned long long>(p) << 32) | (0xFFFFFFFFull - c);
-        } else if (p == t) {
-          ++ties;
+      for (int cc = c0; cc < c1; cc += kU) {
+        uint32_t jv[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) jv[u] = cc + u < c1 ? __ldcg(srow + cc + u) : 0u;
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int c = cc + u;
+          if (c >= c1) break;
+          const uint32_t p = ptab[jv[u]];
+          if (p > t) {
+            const uint32_t slot = atomicAdd(&lcn, 1u);
+            if (slot < kSampMaxK) lc[slot] = (static_cast<unsigned long long>(p) << 32) | (0xFFFFFFFFull - c);
+          } else if (p == t) {
+            ++ties;
+          }
         }
       }
       // exclusive prefix of the tie counts over threads (thread order = column order)
@@ -344,26 +433,39 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
       __syncthreads();
       const uint32_t lim = ltn;
       uint32_t rank = scan[tid >> 5] + incl - ties;  // local rank among this CTA's ties
-      for (int c = c0; c < c1 && rank < lim; ++c) {
-        if (ptab[__ldcg(srow + c)] == t) {
-          lt[rank] = (static_cast<unsigned long long>(t) << 32) | (0xFFFFFFFFull - c);
-          ++rank;
+      for (int cc = c0; cc < c1 && ties > 0 && rank < lim; cc += kU) {
+        uint32_t jv[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) jv[u] = cc + u < c1 ? __ldcg(srow + cc + u) : 0u;
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int c = cc + u;
+          if (c < c1 && rank < lim && ptab[jv[u]] == t) {
+            lt[rank] = (static_cast<unsigned long long>(t) << 32) | (0xFFFFFFFFull - c);
+            ++rank;
+          }
         }
       }
       __syncthreads();
       cluster_sync();  // candidate lists of every rank published
       if (leader) {
-        if (tid == 0) {
-          uint32_t pos = 0;
-          for (int q = 0; q < C; ++q) {
-            const uint32_t n1 = min(ld_cluster_u32(&lcn, q), static_cast<uint32_t>(kSampMaxK));
-            for (uint32_t i = 0; i < n1 && pos < k; ++i) cand[pos++] = ld_cluster_u64(&lc[i], q);
+        // gather the ranks' lists: counts first (one thread per list), then one
+        // thread per candidate, so the remote loads overlap
+        if (tid < 2 * C) {
+          const int q = tid % C;
+          gcnt[tid] = tid < C ? min(ld_cluster_u32(&lcn, q), static_cast<uint32_t>(kSampMaxK))
+                              : ld_cluster_u32(&ltn, q);
+        }
+        __syncthreads();
+        if (tid < static_cast<int>(k)) {
+          uint32_t i = static_cast<uint32_t>(tid), list = 0;
+          while (list < static_cast<uint32_t>(2 * C) && i >= gcnt[list]) i -= gcnt[list++];
+          unsigned long long key = 0;  // unreachable zero when the counts agree
+          if (list < static_cast<uint32_t>(2 * C)) {
+            const uint32_t q = list % C;
+            key = list < static_cast<uint32_t>(C) ? ld_cluster_u64(&lc[i], q) : ld_cluster_u64(&lt[i], q);
           }
-          for (int q = 0; q < C; ++q) {
-            const uint32_t n2 = ld_cluster_u32(&ltn, q);
-            for (uint32_t i = 0; i < n2 && pos < k; ++i) cand[pos++] = ld_cluster_u64(&lt[i], q);
-          }
-          for (; pos < k; ++pos) cand[pos] = 0;  // unreachable when the counts agree
+          cand[tid] = key;
         }
         __syncthreads();
         // rank the k candidate keys (distinct: the column is part of the key)
@@ -428,6 +530,51 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
 
 using namespace mb;
 
+// Per device, once: the kernel's shared-memory limit and how many clusters of each
+// size (1 CTA of 1024 threads and 64 KB + static shared memory per SM) fit at once.
+constexpr int kSampMaxDevices = 64;
+struct SampDevice {
+  bool ready = false;
+  int capacity[9] = {};
+};
+static SampDevice g_samp_dev[kSampMaxDevices];
+static std::once_flag g_samp_once[kSampMaxDevices];
+
+static SampDevice& samp_device(int dev) {
+  std::call_once(g_samp_once[dev], [dev] {
+    SampDevice& sd = g_samp_dev[dev];
+    const int smem = 32768 * static_cast<int>(sizeof(uint16_t));
+    if (cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return;
+    }
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    sd.capacity[1] = sms;
+    for (int c = 2; c <= 8; ++c) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(c, 1);
+      cfg.blockDim = dim3(kSampBlock);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = c;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, k_sample, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        n = 0;
+      }
+      sd.capacity[c] = n;
+    }
+    sd.ready = true;
+  });
+  return g_samp_dev[dev];
+}
+
 extern "C" {
 
 size_t mb_sample_workspace_size(int32_t N, int32_t V) {
@@ -463,15 +610,20 @@ int32_t mb_sample_tokens(const void* logits, int32_t logits_f32, int32_t N, int3
   a.scratch = static_cast<uint16_t*>(workspace);
   a.err = dev_err;
   const size_t smem = static_cast<size_t>(size) * sizeof(uint16_t);
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-          cudaSuccess)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kSampMaxDevices) {
+    (void)cudaGetLastError();
     return MB_ERR_LAUNCH;
-  // cluster size: up to 8 CTAs per row while the rows' clusters fit the GPU at once
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  (void)cudaGetLastError();
-  const int C = std::max(1, std::min(8, sms / N));
+  }
+  SampDevice& sd = samp_device(dev);
+  if (!sd.ready) return MB_ERR_LAUNCH;
+  // cluster size: the largest C <= 8 whose N clusters are resident at once (one wave)
+  int C = 1;
+  for (int c = 8; c >= 2; --c)
+    if (sd.capacity[c] >= N) {
+      C = c;
+      break;
+    }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(C, N);
   cfg.blockDim = dim3(kSampBlock);
