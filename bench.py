@@ -465,13 +465,16 @@ def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 64):
     from moat_b200.decode import DecoderConfig, Int4Decoder, timed_decode
     cfg = DecoderConfig()
     N, P = 16, 512
-    dec = Int4Decoder(cfg, N, device=dev, seed=SEED + 5, rank=rank, world=world)
+    dec = Int4Decoder(cfg, N, device=dev, seed=SEED + 5, rank=rank, world=world, exchange_timeout_s=2.0)
     try:
         dec.fill_prompt_cache(P, seed=SEED + 6)
         g = torch.Generator(device=dev)
         g.manual_seed(SEED + 7)
         dec.ids.copy_(torch.randint(0, cfg.vocab, (N,), generator=g, device=dev, dtype=torch.int32))
-        ms = timed_decode(dec, steps, warmup=3, graph=True)
+        try:
+            ms = timed_decode(dec, steps, warmup=3, graph=True)
+        except RuntimeError as e:  # raised on every rank alike (the check is all-reduced)
+            return {"workload": "BASELINE config 5 decode", "error": str(e), "tensor_parallel": world}
         err = int(dec.err.item())
         wbytes = sum(sum(int(lw[k].numel()) for k in ("wqkv", "wo", "wgu", "wd")) for lw in dec.layers) \
             + int(dec.lm_head.numel())

@@ -339,6 +339,13 @@ def timed_decode(dec: Int4Decoder, steps: int, warmup: int = 3, graph: bool = Tr
     when the decoder is tensor-parallel."""
     t = _lib.torch()
     dec.step(dec.ids)
+    if dec.world > 1:  # every rank learns whether an exchange wait expired before timing
+        import torch.distributed as dist
+        e = dec.err.clone()
+        dist.all_reduce(e, op=dist.ReduceOp.MAX, group=dec.group)
+        if int(e.item()) & 1:
+            raise RuntimeError("tensor-parallel exchange timed out on the first step (device error word %d)"
+                               % int(e.item()))
     if graph:
         dec.capture()
     step = dec.step_graphed if graph else (lambda: dec.step(dec.ids))
