@@ -28,11 +28,13 @@ kernel per join: peer stores over NVLink, then the residual add and RMSNorm; the
 default) or ``"nccl"`` (``all_reduce``, then ``mb_add_rmsnorm``); the greedy choice
 over the split vocabulary is one 64-bit key per shard, maximised across ranks.
 
-``temperature > 0`` (one GPU) replaces the greedy choice by ``mb_sample_tokens``: a
-draw from the top-50 of the exp-LUT softmax of the scaled logits, as the reference's
+``temperature > 0`` replaces the greedy choice by ``mb_sample_tokens``: a draw from
+the top-50 of the exp-LUT softmax of the scaled logits, as the reference's
 ``sample_tokens`` (``batch_generator.py:187-253``), with the random stream's counter
 on the device so the captured step keeps drawing fresh values; ``logprobs`` holds
-each trace's log-probability of its token.
+each trace's log-probability of its token. Tensor-parallel ranks all-gather their
+vocabulary shards (NCCL) and draw with the same seed and counter, so every rank picks
+the same token.
 """
 
 from __future__ import annotations
@@ -106,8 +108,6 @@ class Int4Decoder:
             raise ValueError(f"rank {rank} outside world {world}")
         if exchange not in ("peer", "nccl"):
             raise ValueError("exchange must be 'peer' or 'nccl'")
-        if temperature > 0 and world > 1:
-            raise NotImplementedError("temperature sampling runs on one GPU (the vocabulary is not split)")
         self.rank, self.world, self.group = rank, world, group
         self.exchange, self.peer, self.exchange_timeout_s = exchange, None, exchange_timeout_s
         self.temperature = float(temperature)
@@ -175,6 +175,11 @@ class Int4Decoder:
         if self.temperature > 0:  # top-50 draw from the LUT softmax (range 10), device random stream
             from .sampling import BatchSampler
             self.sampler = BatchSampler(n_traces, V, device=self.dev, seed=sample_seed)
+            if world > 1:  # the vocabulary shards are gathered; every rank draws the same token
+                vmax = max(c1 - c0 for c0, c1 in self.shards["vocab"])
+                self.logits_pad = t.zeros((N, vmax), dtype=f16, device=self.dev)
+                self.logits_all = t.empty((world * N, vmax), dtype=f16, device=self.dev)
+                self.logits_full = t.empty((N, V), dtype=f16, device=self.dev)
         self.length = 0  # positions filled so far (the same for every trace)
         self.graph = None
         nb = int(lib().mb_decode_attn_workspace_size(N, Hl, L, dh))
@@ -307,7 +312,17 @@ class Int4Decoder:
         self._residual_norm(y, self.final_norm, st)
         check(L.mb_int4_gemm(p(self.h), p(self.lm_head), p(self.logits), N, D, V, err, st), "lm_head")
         if self.sampler is not None:
-            self.sampler.sample(self.logits, self.temperature, tokens=self.ids, logprobs=self.logprobs, err=self.err,
+            src = self.logits
+            if self.world > 1:  # all-gather the shards into the whole row on every rank
+                import torch.distributed as dist
+                vmax = self.logits_pad.shape[1]
+                self.logits_pad[:, :V].copy_(self.logits)
+                dist.all_gather_into_tensor(self.logits_all, self.logits_pad, group=self.group)
+                allv = self.logits_all.view(self.world, N, vmax)
+                for r, (c0, c1) in enumerate(self.shards["vocab"]):
+                    self.logits_full[:, c0:c1].copy_(allv[r, :, :c1 - c0])
+                src = self.logits_full
+            self.sampler.sample(src, self.temperature, tokens=self.ids, logprobs=self.logprobs, err=self.err,
                                 stream=st)
         elif self.world == 1:
             check(L.mb_argmax_f16(p(self.logits), N, V, p(self.ids), st), "mb_argmax_f16")
@@ -391,7 +406,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--eager", action="store_true")
-    ap.add_argument("--temperature", type=float, default=0.0, help="> 0: top-50 sampling (one GPU)")
+    ap.add_argument("--temperature", type=float, default=0.0, help="> 0: top-50 sampling")
     ap.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
                     help="how tensor-parallel ranks join their partial products (N > 1)")
     args = ap.parse_args(argv)

@@ -340,3 +340,57 @@ def test_peer_exchange_two_gpus_matches_numpy():
         assert a["ids"].tolist() == ref_ids.tolist() == b["ids"].tolist()
         assert ref_ids[s] == 5
     assert res[0]["err"] == 0 and res[1]["err"] == 0
+
+
+def _tp_sample_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from moat_b200.decode import Int4Decoder
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    tp = None
+    try:
+        tp = Int4Decoder(_small_cfg(), 4, device=dev, seed=11, rank=rank, world=world, exchange_timeout_s=2.0,
+                         temperature=0.8, sample_seed=5)
+        tp.fill_prompt_cache(20, seed=12)
+        tp.ids.copy_(torch.tensor([3, 1000, 4095, 17], dtype=torch.int32, device=dev))
+        recs = []
+        for c in range(3):  # an eager step, then graph replays
+            if c == 0:
+                tp.step(tp.ids)
+            else:
+                if c == 1:
+                    tp.capture()
+                tp.step_graphed()
+            torch.cuda.synchronize()
+            recs.append({"ids": tp.ids.cpu().numpy().copy(), "lp": tp.logprobs.cpu().numpy().copy(),
+                         "logits": tp.logits_full.float().cpu().numpy(), "err": int(tp.err.item())})
+        q.put((rank, recs))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    finally:
+        if tp is not None:
+            tp.close()
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+def test_tp_sampled_decode_two_gpus():
+    """Temperature sampling with the vocabulary split over two ranks: both ranks gather
+    the same logits and draw the same token, the oracle's draw from those logits with
+    the device stream's uniforms (counter = step)."""
+    _needs_two_gpus()
+    from oracle import attention as OA
+    res = _spawn(_tp_sample_worker, 2)
+    table = OA.exp_table(32768, 10.0)
+    for c, (a, b) in enumerate(zip(res[0], res[1])):
+        assert a["err"] == 0 and b["err"] == 0
+        np.testing.assert_array_equal(a["logits"], b["logits"])
+        np.testing.assert_array_equal(a["ids"], b["ids"])
+        otok, olp = S.sample_tokens(a["logits"].astype(np.float16), 0.8, table, 10.0, S.uniforms(5, c, 4))
+        np.testing.assert_array_equal(a["ids"], otok)
+        np.testing.assert_allclose(a["lp"], olp, rtol=1e-6, atol=1e-6)
