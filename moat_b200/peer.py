@@ -58,7 +58,7 @@ class PeerExchange:
             check(L.mb_ipc_alloc(self.nbytes, ctypes.byref(self._own), handle), "mb_ipc_alloc")
         handles = [None] * self.world
         dist.all_gather_object(handles, bytes(handle), group=group)
-        ptrs = []
+        ptrs, failure = [], None
         try:
             with t.cuda.device(self.dev):
                 for q, hq in enumerate(handles):
@@ -70,9 +70,14 @@ class PeerExchange:
                     check(L.mb_ipc_open(hb, ctypes.byref(p)), f"mb_ipc_open(rank {q})")
                     self._opened.append(p.value)
                     ptrs.append(p.value)
-        except Exception:
+        except Exception as e:  # reported to every rank below, so all of them raise together
+            failure = f"rank {self.rank}: {e}"
+        failures = [None] * self.world
+        dist.all_gather_object(failures, failure, group=group)
+        failures = [f for f in failures if f]
+        if failures:
             self.close(barrier=False)
-            raise
+            raise RuntimeError("peer exchange could not map the other ranks' buffers: " + "; ".join(failures))
         self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
         # {epoch, arrivals} per exchange kind: [0:2] add_rmsnorm, [2:4] argmax
         self.state = t.zeros(4, dtype=t.int32, device=self.dev)
