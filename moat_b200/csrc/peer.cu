@@ -28,6 +28,11 @@
 // small local state array (not shared) and is advanced by the last CTA of each call,
 // which keeps a captured CUDA graph replayable.
 //
+// Both kernels are chained with programmatic dependent launch: each waits for the
+// previous kernel to finish before it reads anything (griddepcontrol.wait), then lets
+// the next kernel start its prologue, which itself waits for this grid before it reads
+// x, h or ids; all CTAs of an exchange are resident before a dependent grid launches.
+//
 // Every wait is bounded by the global timer: on expiry the kernel sets
 // MB_DEVERR_TIMEOUT in dev_err and carries on (its outputs are then undefined).
 // Ranks must run on distinct GPUs: two ranks' kernels waiting on each other are never
@@ -130,6 +135,8 @@ __global__ void __launch_bounds__(kPeerBlock) k_peer_add_rmsnorm(PeerSet ps, con
                                                                  uint32_t* state, uint32_t* err) {
   extern __shared__ float delta[];  // [D]: the all-reduced row, fp16-rounded, as float
   __shared__ float part[kPeerBlock / 32];
+  pdl_wait();               // the partial and the epoch state come from earlier kernels
+  pdl_launch_dependents();  // the next kernel's prologue may overlap; it waits for this grid before reading x, h
   const int n = blockIdx.x;
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(state) + 1u;
   const int par = epoch & 1u;
@@ -190,6 +197,8 @@ __global__ void __launch_bounds__(kPeerBlock) k_peer_argmax(PeerSet ps, const ui
                                                             int col0, int32_t* __restrict__ ids, uint32_t* state,
                                                             uint32_t* err) {
   __shared__ unsigned long long best_w[kPeerBlock / 32];
+  pdl_wait();
+  pdl_launch_dependents();
   const int n = blockIdx.x;
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(state) + 1u;
   const int par = epoch & 1u;
@@ -322,9 +331,8 @@ int32_t mb_peer_add_rmsnorm(void* const* bufs, int32_t world, int32_t rank, int6
       cudaFuncSetAttribute(k_peer_add_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
           cudaSuccess)
     return MB_ERR_LAUNCH;
-  k_peer_add_rmsnorm<<<N, kPeerBlock, smem, static_cast<cudaStream_t>(stream)>>>(ps, partial, x, w, D, eps, h, state,
-                                                                                 dev_err);
-  return launch_status();
+  return launch_with_pdl(k_peer_add_rmsnorm, dim3(N), dim3(kPeerBlock), smem, static_cast<cudaStream_t>(stream), ps,
+                         partial, x, w, D, eps, h, state, dev_err);
 }
 
 int32_t mb_peer_argmax(void* const* bufs, int32_t world, int32_t rank, int64_t slot_elems, int64_t timeout_ns,
@@ -335,8 +343,8 @@ int32_t mb_peer_argmax(void* const* bufs, int32_t world, int32_t rank, int64_t s
     return MB_ERR_ARGS;
   PeerSet ps;
   if (!make_peer_set(bufs, world, rank, slot_elems, timeout_ns, &ps)) return MB_ERR_ARGS;
-  k_peer_argmax<<<N, kPeerBlock, 0, static_cast<cudaStream_t>(stream)>>>(ps, logits, V, col0, ids, state, dev_err);
-  return launch_status();
+  return launch_with_pdl(k_peer_argmax, dim3(N), dim3(kPeerBlock), 0, static_cast<cudaStream_t>(stream), ps, logits,
+                         V, col0, ids, state, dev_err);
 }
 
 }  // extern "C"
