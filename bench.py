@@ -488,12 +488,30 @@ def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 64):
         dec.close()  # graph and exchange buffers go before the process group
     del dec
     torch.cuda.empty_cache()
+    replicas = None
+    if world > 1:  # the other way to use N GPUs: every GPU decodes its own 16 traces
+        import torch.distributed as dist
+        rep = Int4Decoder(cfg, N, device=dev, seed=SEED + 5)
+        try:
+            rep.fill_prompt_cache(P, seed=SEED + 6)
+            rep.ids.copy_(torch.randint(0, cfg.vocab, (N,), generator=g, device=dev, dtype=torch.int32))
+            rms = timed_decode(rep, steps, warmup=3, graph=True)
+        finally:
+            rep.close()
+        m = torch.tensor([rms], dtype=torch.float64, device=dev)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        rms = float(m.item())
+        replicas = {"tok_per_s": world * N / rms * 1e3, "ms_per_step": rms, "traces_per_gpu": N,
+                    "scaling": "weak", "note": "independent full-model replicas, no collective; max over ranks"}
+        del rep
+        torch.cuda.empty_cache()
     return {"workload": "BASELINE config 5: 24-layer INT4 decoder, hidden 2048, 16x128 heads, FFN 5504, "
                         "vocab 151936; 16 traces, 512-position cache, greedy", "metric": "decode tok/s",
             "tok_per_s": N / ms * 1e3, "ms_per_step": ms, "steps": steps, "graph": True,
             "tensor_parallel": world, "scaling": "strong" if world > 1 else None,
             "exchange": "NVLink peer stores (mb_peer_add_rmsnorm, mb_peer_argmax)" if world > 1 else None,
             "bytes_per_step": step_bytes, "GBps": step_bytes / ms / 1e6, "device_error_bits": err,
+            "replicas": replicas,
             "data": "synthetic (random-init weights quantized to INT4; KV cache seeded N(0,1))"}
 
 
