@@ -197,6 +197,59 @@ __device__ __forceinline__ void red_add_v2(float* addr, float a, float b) {
 
 
 // ---------------------------------------------------------------------------
+// Greedy-choice keys (numpy.argmax rules over fp16: NaN largest, -0 == +0, ties to
+// the first column): key = code << 32 | (0xFFFFFFFF - column), code an order-preserving
+// 16-bit image of the value, so the largest key names the argmax.
+__device__ __forceinline__ uint32_t argmax_code16(uint16_t h) {
+  if ((h & 0x7C00u) == 0x7C00u && (h & 0x03FFu)) return 0xFFFFu;
+  if (h == 0x8000u) h = 0;
+  return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
+}
+
+__device__ __forceinline__ unsigned long long argmax_key16(uint16_t h, int col) {
+  return (static_cast<unsigned long long>(argmax_code16(h)) << 32) | (0xFFFFFFFFull - static_cast<uint32_t>(col));
+}
+
+// This thread's best key over row[0, V) (global columns col0 + c), thread `tid` of `nt`:
+// 16-byte loads issued four at a time when the row is 16-byte aligned, scalar otherwise.
+__device__ __forceinline__ unsigned long long thread_best_key(const uint16_t* __restrict__ row, int V, int col0,
+                                                              int tid, int nt) {
+  unsigned long long best = 0;
+  int c_tail = 0;
+  if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    const int nv = V >> 3;
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+    for (int i0 = tid; i0 < nv; i0 += 4 * nt) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * nt;
+        v[u] = i < nv ? __ldg(rv + i) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * nt;
+        if (i < nv) {
+          const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const unsigned long long k0 = argmax_key16(static_cast<uint16_t>(w[j] & 0xFFFFu), col0 + 8 * i + 2 * j);
+            const unsigned long long k1 = argmax_key16(static_cast<uint16_t>(w[j] >> 16), col0 + 8 * i + 2 * j + 1);
+            best = k0 > best ? k0 : best;
+            best = k1 > best ? k1 : best;
+          }
+        }
+      }
+    }
+    c_tail = nv << 3;
+  }
+  for (int c = c_tail + tid; c < V; c += nt) {
+    const unsigned long long k = argmax_key16(row[c], col0 + c);
+    best = k > best ? k : best;
+  }
+  return best;
+}
+
 // Thread-block cluster helpers (distributed shared memory)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {

@@ -118,75 +118,10 @@ __global__ void __launch_bounds__(kRowBlock) k_swiglu(const uint16_t* __restrict
 }
 
 // ids[n] = first index of the largest logit of row n (a NaN counts as the largest,
-// like numpy.argmax). One CTA per row.
-__global__ void __launch_bounds__(kRowBlock) k_argmax(const uint16_t* __restrict__ logits, int V,
-                                                      int32_t* __restrict__ ids) {
-  __shared__ float bv[kRowBlock];
-  __shared__ int bi[kRowBlock];
-  pdl_wait();
-  pdl_launch_dependents();
-  const int n = blockIdx.x;
-  const uint16_t* row = logits + static_cast<int64_t>(n) * V;
-  float best = -INFINITY;
-  int besti = 0x7fffffff;
-  for (int c = threadIdx.x; c < V; c += kRowBlock) {
-    const float v = __half2float(__ushort_as_half(row[c]));
-    const bool nan_v = v != v, nan_b = best != best;
-    if (besti == 0x7fffffff || (nan_v && !nan_b) || (!nan_b && v > best)) {
-      best = v;
-      besti = c;
-    }
-  }
-  bv[threadIdx.x] = best;
-  bi[threadIdx.x] = besti;
-  __syncthreads();
-  for (int s = kRowBlock / 2; s; s >>= 1) {
-    if (threadIdx.x < s) {
-      const float a = bv[threadIdx.x], b = bv[threadIdx.x + s];
-      const int ia = bi[threadIdx.x], ib = bi[threadIdx.x + s];
-      const bool na = a != a, nb = b != b;
-      bool take_b;
-      if (ib == 0x7fffffff) take_b = false;
-      else if (ia == 0x7fffffff) take_b = true;
-      else if (na != nb) take_b = nb;                 // NaN wins
-      else if (na) take_b = ib < ia;                  // both NaN: first index
-      else take_b = (b > a) || (b == a && ib < ia);   // larger, ties to the first index
-      if (take_b) {
-        bv[threadIdx.x] = b;
-        bi[threadIdx.x] = ib;
-      }
-    }
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) ids[n] = bi[0] == 0x7fffffff ? 0 : bi[0];
-}
+// -0 equals +0, like numpy.argmax). One CTA of 1024 threads per row.
+constexpr int kArgBlock = 1024;
 
-// Order-preserving 16-bit code of an fp16 logit under the argmax rules above: every
-// NaN is the largest code, -0 and +0 share one code (equal values), and otherwise a
-// larger value has a larger code.
-__device__ __forceinline__ uint32_t argmax_code(uint16_t h) {
-  if ((h & 0x7C00u) == 0x7C00u && (h & 0x03FFu)) return 0xFFFFu;
-  if (h == 0x8000u) h = 0;
-  return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
-}
-
-// One row shard of a column-split vocabulary: the shard's best logit as a 64-bit key,
-// code << 32 | (0xFFFFFFFF - global column). The largest key over all shards is the
-// global argmax with ties to the first column, so the shards combine with one integer
-// MAX all-reduce.
-__global__ void __launch_bounds__(kRowBlock) k_argmax_key(const uint16_t* __restrict__ logits, int V, int col0,
-                                                          int64_t* __restrict__ keys) {
-  __shared__ unsigned long long best_w[kRowBlock / 32];
-  pdl_wait();
-  pdl_launch_dependents();
-  const int n = blockIdx.x;
-  const uint16_t* row = logits + static_cast<int64_t>(n) * V;
-  unsigned long long best = 0;
-  for (int c = threadIdx.x; c < V; c += kRowBlock) {
-    const unsigned long long key = (static_cast<unsigned long long>(argmax_code(row[c])) << 32) |
-                                   (0xFFFFFFFFull - static_cast<unsigned long long>(col0 + c));
-    best = key > best ? key : best;
-  }
+__device__ __forceinline__ unsigned long long block_best_key(unsigned long long best, unsigned long long* best_w) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
@@ -194,10 +129,35 @@ __global__ void __launch_bounds__(kRowBlock) k_argmax_key(const uint16_t* __rest
   }
   if ((threadIdx.x & 31) == 0) best_w[threadIdx.x >> 5] = best;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < kRowBlock / 32; ++w) best = best_w[w] > best ? best_w[w] : best;
-    keys[n] = static_cast<int64_t>(best);
-  }
+  if (threadIdx.x == 0)
+    for (int w = 1; w < kArgBlock / 32; ++w) best = best_w[w] > best ? best_w[w] : best;
+  return best;  // the row's best key in thread 0
+}
+
+__global__ void __launch_bounds__(kArgBlock) k_argmax(const uint16_t* __restrict__ logits, int V,
+                                                      int32_t* __restrict__ ids) {
+  __shared__ unsigned long long best_w[kArgBlock / 32];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int n = blockIdx.x;
+  const unsigned long long best =
+      block_best_key(thread_best_key(logits + static_cast<int64_t>(n) * V, V, 0, threadIdx.x, kArgBlock), best_w);
+  if (threadIdx.x == 0) ids[n] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+}
+
+// One row shard of a column-split vocabulary: the shard's best logit as a 64-bit key,
+// code << 32 | (0xFFFFFFFF - global column). The largest key over all shards is the
+// global argmax with ties to the first column, so the shards combine with one integer
+// MAX all-reduce.
+__global__ void __launch_bounds__(kArgBlock) k_argmax_key(const uint16_t* __restrict__ logits, int V, int col0,
+                                                          int64_t* __restrict__ keys) {
+  __shared__ unsigned long long best_w[kArgBlock / 32];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int n = blockIdx.x;
+  const unsigned long long best =
+      block_best_key(thread_best_key(logits + static_cast<int64_t>(n) * V, V, col0, threadIdx.x, kArgBlock), best_w);
+  if (threadIdx.x == 0) keys[n] = static_cast<int64_t>(best);
 }
 
 __global__ void k_keys_to_ids(const int64_t* __restrict__ keys, int N, int32_t* __restrict__ ids) {
@@ -260,13 +220,13 @@ int32_t mb_swiglu(const uint16_t* gu, int32_t N, int32_t F, uint16_t* a, void* s
 int32_t mb_argmax_f16(const uint16_t* logits, int32_t N, int32_t V, int32_t* ids, void* stream) {
   if (!logits || !ids) return MB_ERR_NULL;
   if (N < 1 || V < 1) return MB_ERR_ARGS;
-  return launch_with_pdl(k_argmax, dim3(N), dim3(kRowBlock), 0, static_cast<cudaStream_t>(stream), logits, V, ids);
+  return launch_with_pdl(k_argmax, dim3(N), dim3(kArgBlock), 0, static_cast<cudaStream_t>(stream), logits, V, ids);
 }
 
 int32_t mb_argmax_key_f16(const uint16_t* logits, int32_t N, int32_t V, int32_t col0, int64_t* keys, void* stream) {
   if (!logits || !keys) return MB_ERR_NULL;
   if (N < 1 || V < 1 || col0 < 0 || static_cast<int64_t>(col0) + V > 0x7FFFFFFFll) return MB_ERR_ARGS;
-  return launch_with_pdl(k_argmax_key, dim3(N), dim3(kRowBlock), 0, static_cast<cudaStream_t>(stream), logits, V,
+  return launch_with_pdl(k_argmax_key, dim3(N), dim3(kArgBlock), 0, static_cast<cudaStream_t>(stream), logits, V,
                          col0, keys);
 }
 

@@ -185,30 +185,21 @@ __global__ void __launch_bounds__(kPeerBlock) k_peer_add_rmsnorm(PeerSet ps, con
   peer_finish(state, epoch);
 }
 
-__device__ __forceinline__ uint32_t peer_argmax_code(uint16_t hb) {
-  if ((hb & 0x7C00u) == 0x7C00u && (hb & 0x03FFu)) return 0xFFFFu;
-  if (hb == 0x8000u) hb = 0;
-  return (hb & 0x8000u) ? (~hb & 0xFFFFu) : (hb | 0x8000u);
-}
-
 // One CTA per row n: key of this rank's best logit, exchanged, max over ranks -> ids[n].
 // state = {epoch, arrivals} of channel 1.
-__global__ void __launch_bounds__(kPeerBlock) k_peer_argmax(PeerSet ps, const uint16_t* __restrict__ logits, int V,
-                                                            int col0, int32_t* __restrict__ ids, uint32_t* state,
-                                                            uint32_t* err) {
-  __shared__ unsigned long long best_w[kPeerBlock / 32];
+constexpr int kPeerArgBlock = 1024;
+
+__global__ void __launch_bounds__(kPeerArgBlock) k_peer_argmax(PeerSet ps, const uint16_t* __restrict__ logits, int V,
+                                                               int col0, int32_t* __restrict__ ids, uint32_t* state,
+                                                               uint32_t* err) {
+  __shared__ unsigned long long best_w[kPeerArgBlock / 32];
   pdl_wait();
   pdl_launch_dependents();
   const int n = blockIdx.x;
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(state) + 1u;
   const int par = epoch & 1u;
-  const uint16_t* row = logits + static_cast<int64_t>(n) * V;
-  unsigned long long best = 0;
-  for (int c = threadIdx.x; c < V; c += kPeerBlock) {
-    const unsigned long long key = (static_cast<unsigned long long>(peer_argmax_code(row[c])) << 32) |
-                                   (0xFFFFFFFFull - static_cast<unsigned long long>(col0 + c));
-    best = key > best ? key : best;
-  }
+  unsigned long long best =
+      thread_best_key(logits + static_cast<int64_t>(n) * V, V, col0, threadIdx.x, kPeerArgBlock);
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
@@ -221,7 +212,7 @@ __global__ void __launch_bounds__(kPeerBlock) k_peer_argmax(PeerSet ps, const ui
   };
   if (threadIdx.x < ps.world) {
     unsigned long long b = best_w[0];
-    for (int i = 1; i < kPeerBlock / 32; ++i) b = best_w[i] > b ? best_w[i] : b;
+    for (int i = 1; i < kPeerArgBlock / 32; ++i) b = best_w[i] > b ? best_w[i] : b;
     *key_slot(ps.buf[threadIdx.x], ps.rank) = b;
   }
   peer_signal_and_wait(ps, 1, n, epoch, err);
@@ -343,7 +334,7 @@ int32_t mb_peer_argmax(void* const* bufs, int32_t world, int32_t rank, int64_t s
     return MB_ERR_ARGS;
   PeerSet ps;
   if (!make_peer_set(bufs, world, rank, slot_elems, timeout_ns, &ps)) return MB_ERR_ARGS;
-  return launch_with_pdl(k_peer_argmax, dim3(N), dim3(kPeerBlock), 0, static_cast<cudaStream_t>(stream), ps, logits,
+  return launch_with_pdl(k_peer_argmax, dim3(N), dim3(kPeerArgBlock), 0, static_cast<cudaStream_t>(stream), ps, logits,
                          V, col0, ids, state, dev_err);
 }
 
