@@ -8,29 +8,28 @@
 //
 // Design (weight streaming, HBM bound):
 //  * The M columns are cut into strips of WS = 256 (one super-block per row) or 128
-//    columns. Each strip is handled by one thread-block cluster of Ck CTAs that
-//    split its K rows; the grid (strips x Ck) is sized to one wave of the SMs. The
-//    split-K partial sums are reduced on chip through distributed shared memory at
-//    the end, so there is no global workspace, no atomics, and the result is
-//    deterministic.
-//  * One producer thread per CTA streams the strip's super-block rows with 3-D TMA
-//    tile loads (cp.async.bulk.tensor, L2 evict-first) into a ring of shared-memory
-//    stages guarded by mbarriers. The weights never depend on the previous kernel,
-//    so the ring is filled before griddepcontrol.wait (programmatic dependent
-//    launch). After it the consumer warps copy the CTA's activation slice (L2
-//    resident) into shared memory with all loads of a round in flight.
-//  * Consumer warps expand nibbles straight into mma.m16n8k16 A fragments in
-//    registers: byte permute + magic-exponent fp16 conversion + one fp16 multiply by
-//    the group scale, bit-exact with the reference dequant; the batch (padded to
-//    8/16/32) is the MMA n dimension, fp32 accumulate.
-//  * Reduction: the k-group warps park their partial tiles in the drained ring and sum
-//    them in a fixed order into a send tile holding one block per owner CTA of the
-//    cluster; one bulk shared-memory copy per peer (cp.async.bulk.shared::cluster)
-//    moves each block, completion counted on the owner's mbarrier, and each owner adds
-//    the Ck blocks of its columns in rank order.
-//  * Shared-memory rows are laid out so the fragment loads are bank-conflict free:
-//    full 144-byte super-block rows (WS = 256), or a 16-byte scale row plus a
-//    nibble row padded to 80 / 96 bytes by the TMA box (WS = 128, M % 256 == 128).
+//    columns. Each strip is handled by one thread-block cluster of Ck CTAs that split
+//    its K rows; the grid (strips x Ck) is one wave of the SMs.
+//  * One producer warp per CTA streams the CTA's super-block rows with 3-D TMA tile
+//    loads (cp.async.bulk.tensor, L2 evict-first, no multicast) into a ring of
+//    shared-memory stages guarded by mbarriers, and re-lays each landed stage's fp16
+//    group scales as (row pair, group) words for the consumers. Weights never depend on
+//    the previous kernel, so the producer starts before griddepcontrol.wait
+//    (programmatic dependent launch); a plan whose CTA fits half an SM lets the next
+//    call's CTA become resident beside this one and fill its ring while this call
+//    finishes.
+//  * Consumer warp w owns one 32-column scale group of the strip (and, for 128-wide
+//    strips, every other 16-row k slice). ldmatrix.trans of the group's nibble rows
+//    gives each lane two bytes of two consecutive k rows in one register, which a
+//    lop3 with the fp16 magic exponent turns into an mma.m16n8k16 A fragment pair
+//    (k, k+1) without any byte permute: exact integers q = n - 8. Every row of an m16
+//    tile lies in one scale group, so the group scale of row k is applied to the
+//    activations instead (B' = fp16(x[n, k] * s[k, g]), two f16x2 multiplies per 16 k
+//    rows and 8 batch rows) and the tensor core sums q * B' in fp32.
+//  * Reduction: every warp stores its partial tile straight into the shared memory of
+//    the cluster CTA that owns those columns (st.shared::cluster), one cluster barrier,
+//    and each owner adds the Ck x (k groups) partials of its columns in a fixed order:
+//    deterministic, no global workspace, no atomics.
 #include <algorithm>
 #include <mutex>
 #include <unordered_map>
@@ -45,33 +44,45 @@ constexpr int kSPS = 8;         // slices per full stage (128 rows)
 constexpr int kStageRows = kSPS * kSliceRows;
 constexpr int kMaxStages = 8;
 constexpr int kMaxCk = 8;
-constexpr int kAhead = 3;  // weight stages in flight per CTA
+constexpr int kAhead = 3;  // weight stages in flight per CTA while the ring first fills
+constexpr int kCW = 16;    // consumer warps per CTA (two or four per scale group)
 
 // Shared-memory layout of one pipeline stage (128 rows of the CTA's strip).
 //  WS = 256: full 144-byte super-block rows (scales then nibbles), row stride 144 B.
-//  WS = 128 / 64: a 16-byte scale row per k row, then the strip's nibble bytes in a
-//  row padded by the TMA box (80 / 48 bytes for one row phase, 96 / 32 bytes for two)
-//  so that the fragment loads below hit 32 distinct banks. With P = 2 row phases
-//  (M % 256 == 128) rows of each phase are stored together.
+//  WS = 128: a 16-byte scale row per k row, then the strip's 64 nibble bytes in a row
+//  padded to 80 bytes by the TMA box. With P = 2 row phases (M % 256 == 128) the rows
+//  of each phase are stored together.
+// Row strides of 144 and 80 bytes put 8 consecutive rows of a region in 8 distinct
+// 16-byte bank groups, so every ldmatrix below is conflict free. For P = 2 the 16 k
+// rows of a slice are read as 8 even rows (one region) then 8 odd rows, which is also
+// the order in which the slice's activations are staged.
 template <int WS, int P>
 struct Layout {
   static_assert(WS == 256 || WS == 128, "strip width");
   static_assert(WS != 256 || P == 1, "a 256-wide strip needs M % 256 == 0");
   static_assert(P == 1 || P == 2, "row phases");
-  static constexpr int kNibRow = (WS == 128) ? (P == 1 ? 80 : 96) : (P == 1 ? 48 : 32);
+  static constexpr int kGS = WS / 32;  // scale groups per strip row
+  static constexpr int kNibRow = 80;
   static constexpr int kScRegion = kStageRows * 16;
   static constexpr int kStageBytes = (WS == 256) ? kStageRows * kSB : kStageRows * (16 + kNibRow);
   static constexpr int kRowsPerPhase = kStageRows / P;
+  static constexpr int kScBytes = kSPS * kGS * 4 * 8;  // re-laid scale pairs of one stage
   static __device__ __host__ constexpr int bytes(int n) {  // tx bytes of a stage with n slices
     return (WS == 256) ? n * kSliceRows * kSB : n * kSliceRows * (16 + kNibRow);
   }
   // byte offset of row k's scale chunk / first strip nibble byte within a stage
-  static __device__ __forceinline__ constexpr int sc(int k) {
+  static __device__ __host__ constexpr int sc(int k) {
     return (WS == 256) ? k * kSB : ((k & (P - 1)) * kRowsPerPhase + k / P) * 16;
   }
-  static __device__ __forceinline__ constexpr int nib(int k) {
+  static __device__ __host__ constexpr int nib(int k) {
     return (WS == 256) ? k * kSB + 16 : kScRegion + ((k & (P - 1)) * kRowsPerPhase + k / P) * kNibRow;
   }
+  // stage row of MMA k index i (0..15) of slice sl
+  static __device__ __host__ constexpr int row_of(int sl, int i) {
+    return P == 1 ? kSliceRows * sl + i : kSliceRows * sl + (i < 8 ? 2 * i : 2 * (i - 8) + 1);
+  }
+  static constexpr int kSliceStride = nib(kSliceRows) - nib(0);  // nibble bytes between slices
+  static constexpr int kScSliceStride = sc(kSliceRows) - sc(0);
 };
 
 struct GemmParams {
@@ -82,100 +93,49 @@ struct GemmParams {
   int KS;               // k slices (ceil(K / 16))
   int Ck;               // CTAs per cluster = K split
   int S;                // stages in the ring
-  int xchunks;          // 128-wide k chunks of the activation slice
-  int xcstride;         // bytes per chunk in shared memory (N rows of kXRow bytes, 128-aligned)
-  int sendoff;          // byte offset of the send tile [Ck][N][cwp] (reuses ring + activations)
+  int xcstride;         // bytes per 128-k chunk of activations (N rows of kXRow bytes, 128-aligned)
+  int scboff;           // byte offset of the re-laid scale pairs [S][kScBytes]
+  int xoff;             // byte offset of the activation chunks
+  int recvoff;          // byte offset of the receive slots [Ck][kKG][N][rp] floats
   int baroff;           // byte offset of the mbarriers
-  int recvoff;          // byte offset of the receive slots [Ck][N][cwp] (outside the ring)
+  int rp;               // floats per receive row (owned columns + 4 pad)
+  int sl_first[kMaxCk + 1];  // k slices [sl_first[q], sl_first[q + 1]) go to CTA q of a cluster
+  int gfirst[kMaxCk + 1];    // CTA q owns strip groups [gfirst[q], gfirst[q + 1])
+  int owner[8];              // the CTA that owns strip group g
 };
 
-// Activations in shared memory: chunks of 128 k values by N rows; a row takes 272
-// bytes (128 values + 8 pad), so consecutive rows start 4 banks apart and the
-// B-fragment loads are conflict free.
-constexpr int kXChunk = 128;
+// Activations in shared memory: chunks of 128 k values (one stage) by N rows; a row
+// takes 272 bytes (128 values + 8 pad), so consecutive rows start 4 banks apart and
+// the B-fragment loads are conflict free.
 constexpr int kXRow = 272;
 
 struct WMaps {  // weight tensor maps: full-stage and 16-row boxes (scale / nibble rows)
   CUtensorMap full_a, full_b, slice_a, slice_b;
 };
 
-// Row stride (floats) of a k-group parking tile: WS columns with 2 pad floats after
-// every MR-column run, and a stride of 4 (mod 16) between batch rows, so the float2
-// stores of a warp's fragments hit distinct banks for MR = 32, 16 and 8.
-template <int WS, int MR>
-struct ParkRow {
-  static constexpr int v = (WS + 2 * WS / MR - 4 + 15) / 16 * 16 + 4;
-};
-
-template <int NW>
-__device__ __forceinline__ void lds_words(const uint8_t* p, uint32_t (&w)[NW]) {
-  if constexpr (NW == 4) {
-    const uint4 v = *reinterpret_cast<const uint4*>(p);
-    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-  } else if constexpr (NW == 2) {
-    const uint2 v = *reinterpret_cast<const uint2*>(p);
-    w[0] = v.x; w[1] = v.y;
-  } else {
-    w[0] = *reinterpret_cast<const uint32_t*>(p);
-  }
+// Shared-memory loads by 32-bit shared-window address, so the loop's address arithmetic
+// stays in 32-bit registers with constant offsets.
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
 }
-__device__ __forceinline__ uint32_t lds_u32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
-__device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+__device__ __forceinline__ uint2 ld_shared_v2(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
 
-// One 16-row k slice for this thread's MR-column run.
-// Thread (g4 = lane/4, t4 = lane%4) owns rows 2t4, 2t4+1, 2t4+8, 2t4+9 of the slice
-// (the k positions of the m16n8k16 A fragment) and MR consecutive columns; m16 tile
-// i of the warp maps fragment row g4 to column 2i and row g4+8 to column 2i+1 of the
-// run, so each nibble byte feeds exactly one tile and the warp has MR/2 independent
-// accumulator chains per batch tile. The weight operand is fp16((n - 8) * s): exact
-// magic-exponent conversion of the nibble, then one rounding multiply by the group
-// scale — bit-identical to the reference dequant.
-//   stage, k0: stage base and the stage-local row 2t4 of this slice; nb: byte offset
-//   of the run within a nibble row; ge / go: scale index for even / odd rows;
-//   xrow: this lane's activation row (n = 8 nt + g4) at the slice's first k.
-template <int NT, int WS, int P, int MR>
-__device__ __forceinline__ void consume_slice(const uint8_t* stage, int k0, int nb, int ge, int go,
-                                              const uint8_t* const (&xrow)[NT], const bool (&xok)[NT], int t4,
-                                              float (&acc)[MR / 2][NT][4]) {
-  using L = Layout<WS, P>;
-  constexpr int NW = MR / 8;  // 32-bit nibble words per row
-  // rows 2t4, 2t4+1, 2t4+8, 2t4+9 as constant offsets from row 2t4
-  constexpr int dn1 = L::nib(1) - L::nib(0), dn8 = L::nib(8) - L::nib(0), dn9 = L::nib(9) - L::nib(0);
-  constexpr int ds1 = L::sc(1) - L::sc(0), ds8 = L::sc(8) - L::sc(0), ds9 = L::sc(9) - L::sc(0);
-  const uint8_t* pn = stage + L::nib(k0) + nb;
-  const uint8_t* ps = stage + L::sc(k0);
-  uint32_t w0[NW], w1[NW], w2[NW], w3[NW];
-  lds_words<NW>(pn, w0);
-  lds_words<NW>(pn + dn1, w1);
-  lds_words<NW>(pn + dn8, w2);
-  lds_words<NW>(pn + dn9, w3);
-  const uint32_t s01 = lds_u16(ps + 2 * ge) | (lds_u16(ps + ds1 + 2 * go) << 16);
-  const uint32_t s23 = lds_u16(ps + ds8 + 2 * ge) | (lds_u16(ps + ds9 + 2 * go) << 16);
-  uint32_t bf[NT][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    bf[nt][0] = xok[nt] ? lds_u32(xrow[nt] + 4 * t4) : 0u;
-    bf[nt][1] = xok[nt] ? lds_u32(xrow[nt] + 16 + 4 * t4) : 0u;
-  }
-#pragma unroll
-  for (int v = 0; v < NW; ++v) {
-    const uint32_t p01l = prmt(w0[v], w1[v], 0x5410u), p01h = prmt(w0[v], w1[v], 0x7632u);
-    const uint32_t p23l = prmt(w2[v], w3[v], 0x5410u), p23h = prmt(w2[v], w3[v], 0x7632u);
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const uint32_t q01 = ((b & 2) ? p01h : p01l) >> (8 * (b & 1));
-      const uint32_t q23 = ((b & 2) ? p23h : p23l) >> (8 * (b & 1));
-      uint32_t a0, a1, a2, a3;
-      nibbles_to_half2(q01, a0, a1);
-      nibbles_to_half2(q23, a2, a3);
-      a0 = hmul2(a0, s01);
-      a1 = hmul2(a1, s01);
-      a2 = hmul2(a2, s23);
-      a3 = hmul2(a3, s23);
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) mma_16816(acc[4 * v + b][nt], a0, a1, a2, a3, bf[nt][0], bf[nt][1]);
-    }
-  }
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
 }
 
 template <int WS, int P>
@@ -210,56 +170,118 @@ __device__ __forceinline__ void issue_stage(const WMaps& maps, uint8_t* dst, uin
   }
 }
 
-__device__ __forceinline__ void store_half2(uint16_t* dst, float a, float b) {
-  const __half2 x = __floats2half2_rn(a, b);
-  *reinterpret_cast<uint32_t*>(dst) = *reinterpret_cast<const uint32_t*>(&x);
+// Producer warp: the landed stage's scales -> [slice][group][t4] words of two half2
+// pairs: (s[row(2 t4)], s[row(2 t4 + 1)]) and (s[row(2 t4 + 8)], s[row(2 t4 + 9)]) of
+// the strip's group, the pairs a consumer lane multiplies its B fragments by.
+// ldmatrix.trans of 8 scale rows gives lane (g4, t4) the scales of super-block group g4
+// of rows (2 t4, 2 t4 + 1); grp_m is the first super-block group of the strip in rows
+// of MMA half m (the row phase for P = 2).
+template <int WS, int P>
+__device__ __forceinline__ void relay_scales(const uint8_t* stage, uint8_t* scs, int lane, int grp0, int grp1) {
+  using L = Layout<WS, P>;
+  constexpr int GS = L::kGS;
+  const int g4 = lane >> 2, t4 = lane & 3;
+  const int mm = lane >> 3, j8 = lane & 7;
+  // matrix mm of an x4: slice 2 pr + (mm >> 1), MMA half m = mm & 1, row j8 of that half
+  const uint32_t a0 = smem_u32(stage) + L::sc(L::row_of(mm >> 1, 8 * (mm & 1) + j8));
+#pragma unroll
+  for (int pr = 0; pr < kSPS / 2; ++pr) {
+    uint32_t r[4];
+    ldsm_x4_trans(a0 + 2 * pr * L::kScSliceStride, r[0], r[1], r[2], r[3]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int sl = 2 * pr + (i >> 1), m = i & 1;
+      const int gl = g4 - (m ? grp1 : grp0);
+      if (gl >= 0 && gl < GS)
+        *reinterpret_cast<uint32_t*>(scs + ((sl * GS + gl) * 4 + t4) * 8 + 4 * m) = r[i];
+    }
+  }
 }
 
-// Columns per thread run for (NT, WS): 32 / NT, at most WS / 8 (eight runs per warp).
-template <int NT, int WS>
-struct RunCols {
-  static constexpr int v = (32 / NT < WS / 8) ? 32 / NT : WS / 8;
+// The nibble -> fp16 constants of the dequant loop, held in registers for the whole
+// kernel (made opaque to the compiler once, so they are not re-created at every use).
+struct NibConst {
+  uint32_t lo_mask, hi_mask, magic, sub_lo, mul_hi, add_hi;
+  __device__ __forceinline__ NibConst()
+      : lo_mask(0x000F000Fu), hi_mask(0x00F000F0u), magic(0x64006400u), sub_lo(0x64086408u), mul_hi(0x2C002C00u),
+        add_hi(0xD480D480u) {
+    asm volatile("" : "+r"(lo_mask), "+r"(hi_mask), "+r"(magic), "+r"(sub_lo), "+r"(mul_hi), "+r"(add_hi));
+  }
 };
 
-// NT: n-tiles of 8 batch rows (1, 2, 4); WS: strip width; P: row phases (1, 2);
-// CW: consumer warps; MINB: CTAs per SM the plan wants resident -- 2 leaves room for
-// the next call's CTA (launched early through PDL) to prefetch, 1 gives a CTA that
-// has the SM to itself the registers for a deeper instruction schedule.
-template <int NT, int WS, int P, int CW, int MINB>
-__global__ void __launch_bounds__((CW + 1) * 32, MINB)
+// nibbles_to_half2 with the constants in registers: low nibbles of bytes 0 / 2 of p ->
+// (n0 - 8, n2 - 8), high nibbles -> (h0 - 8, h2 - 8), exact.
+__device__ __forceinline__ void nib2h(const NibConst& c, uint32_t p, uint32_t& lo, uint32_t& hi) {
+  const uint32_t l = lop3<0xEA>(p, c.lo_mask, c.magic);
+  const uint32_t h = lop3<0xEA>(p, c.hi_mask, c.magic);
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(l), "r"(c.sub_lo));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(hi) : "r"(h), "r"(c.mul_hi), "r"(c.add_hi));
+}
+
+__device__ __forceinline__ void store_half4(uint16_t* dst, float a, float b, float c, float d) {
+  const __half2 x = __floats2half2_rn(a, b), y = __floats2half2_rn(c, d);
+  uint2 v;
+  v.x = *reinterpret_cast<const uint32_t*>(&x);
+  v.y = *reinterpret_cast<const uint32_t*>(&y);
+  *reinterpret_cast<uint2*>(dst) = v;
+}
+
+// One 16-row slice of this warp's group (xr: the lane's activation words of the slice,
+// k indices 2 t4 and 2 t4 + 8 at +0 / +16): r0 / r1 are lane (g4, t4)'s ldmatrix words of
+// MMA k halves 0 / 1 (bytes 2 g4, 2 g4 + 1 of rows 2 t4, 2 t4 + 1 of the half). Tile 0
+// maps fragment row g4 to group column 4 g4 and row g4 + 8 to column 4 g4 + 1 (low /
+// high nibble of byte 2 g4); tile 1 takes columns 4 g4 + 2 and 4 g4 + 3 (byte 2 g4 + 1).
+template <int NT>
+__device__ __forceinline__ void consume_slice(const NibConst& kc, uint32_t r0, uint32_t r1, const uint32_t (&xr)[NT],
+                                              uint2 sc, float (&acc)[2][NT][4]) {
+  uint32_t bp[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const uint32_t b0 = ld_shared_u32(xr[nt]);
+    const uint32_t b1 = ld_shared_u32(xr[nt] + 16);
+    bp[nt][0] = hmul2(b0, sc.x);
+    bp[nt][1] = hmul2(b1, sc.y);
+  }
+  uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
+  nib2h(kc, r0, a0, a1);
+  nib2h(kc, r1, a2, a3);
+  nib2h(kc, r0 >> 8, c0, c1);
+  nib2h(kc, r1 >> 8, c2, c3);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    mma_16816(acc[0][nt], a0, a1, a2, a3, bp[nt][0], bp[nt][1]);
+    mma_16816(acc[1][nt], c0, c1, c2, c3, bp[nt][0], bp[nt][1]);
+  }
+}
+
+// NT: n-tiles of 8 batch rows (1, 2, 4); WS: strip width; P: row phases (1, 2).
+// One CTA per SM (16 consumer warps take the SM's registers).
+template <int NT, int WS, int P>
+__global__ void __launch_bounds__((kCW + 1) * 32, 1)
     k_gemm_int4(const __grid_constant__ WMaps maps, const GemmParams p) {
   using L = Layout<WS, P>;
-  constexpr int MR = RunCols<NT, WS>::v;  // columns per thread run
-  constexpr int kTiles = MR / 2;          // m16 tiles per warp
-  constexpr int kCm = WS / (8 * MR);      // column parts per strip (one warp each)
-  constexpr int kKG = CW / kCm;           // warps sharing a column part (k groups)
-  static_assert(kCm * kKG == CW, "warp layout");
-  constexpr int kRow = ParkRow<WS, MR>::v;
+  constexpr int GS = L::kGS;
+  constexpr int kKG = kCW / GS;  // warps per group (k groups): 2 for WS = 256, 4 for WS = 128
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base, derived from the shared array itself so that every access
   // below compiles to a shared-memory (not generic) load or store
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* stages = smem;
-  uint8_t* xs = stages + p.S * L::kStageBytes;
+  uint8_t* scb = smem + p.scboff;
+  uint8_t* xs = smem + p.xoff;
+  float* recv = reinterpret_cast<float*>(smem + p.recvoff);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.baroff);
   uint64_t* empty = full + kMaxStages;
-  uint64_t* rbar = empty + kMaxStages;  // the peers' partial sums of this CTA's columns landed
+  uint64_t* ready = empty + kMaxStages;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int strip = blockIdx.x / p.Ck;
   const int q = blockIdx.x - strip * p.Ck;  // == rank in the cluster (cluster dims = (Ck,1,1))
-  const int sl0 = static_cast<int>((static_cast<long long>(q) * p.KS) / p.Ck);
-  const int sl1 = static_cast<int>((static_cast<long long>(q + 1) * p.KS) / p.Ck);
+  const int sl0 = p.sl_first[q], sl1 = p.sl_first[q + 1];
   const int nst = (sl1 - sl0 + kSPS - 1) / kSPS;
   const int c0 = strip * WS;
-  // CTA q of the cluster owns columns [q cw, min((q + 1) cw, WS)) of the strip:
-  // ceil(WS / Ck) rounded up to even, so col / cw < Ck for every column. Partial sums
-  // travel in blocks of N rows x cwp floats (a multiple of 16 bytes).
-  const int cw = ((WS + p.Ck - 1) / p.Ck + 1) & ~1;
-  const int cwp = (cw + 3) & ~3;
-  const uint32_t blk = static_cast<uint32_t>(p.N * cwp * 4);
   // per row phase: super-block index within a period (y), first nibble byte of the
-  // strip in that super-block (x) and the scale index of the strip's first column
+  // strip in that super-block (x) and the super-block group of the strip's first column
   int ey[P], ex[P], grp[P];
 #pragma unroll
   for (int r = 0; r < P; ++r) {
@@ -273,40 +295,58 @@ __global__ void __launch_bounds__((CW + 1) * 32, MINB)
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.S; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(empty + s, CW);
+      mbar_init(empty + s, kCW);
+      mbar_init(ready + s, 32);
     }
-    mbar_init(rbar, 1);
     fence_mbar_init();
-    // this CTA's own arrival: the phase completes when the Ck - 1 peer blocks land
-    if (p.Ck > 1) mbar_expect_tx(rbar, static_cast<uint32_t>(p.Ck - 1) * blk);
   }
   __syncthreads();
-  if (p.Ck > 1) cluster_arrive();  // phase 0: the barriers above exist (awaited before any copy)
+  // phase 0 of the cluster barrier: every CTA of the cluster has started (awaited
+  // before the first store into a peer's shared memory)
+  if (p.Ck > 1) cluster_arrive_relaxed();
   pdl_launch_dependents();
 
-  if (warp == CW) {
+  if (warp == kCW) {
     // ---------------- producer ----------------
-    if (lane == 0) {
-      // weights never depend on the previous grid: no griddepcontrol.wait here, so the
-      // ring fills while the previous grid finishes
-      const uint64_t pol = policy_evict_first();
-      for (int st = 0; st < nst; ++st) {
-        const int s = st % p.S;
-        // at most kAhead stages in flight: the memory system then returns this CTA's
-        // stages in order, so the first one lands early instead of with the last (with
-        // kAhead <= S the slot of stage st - kAhead is not reused yet, so its parity is
-        // unambiguous; with a shorter ring the empty wait below already implies it)
-        if (st >= kAhead && kAhead <= p.S) {
-          const int sa = st - kAhead;
-          if (!mbar_wait(full + sa % p.S, (sa / p.S) & 1) && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
+    // weights never depend on the previous grid: no griddepcontrol.wait here, so the
+    // ring fills (and its scales are re-laid) while the previous grid finishes
+    const uint64_t pol = policy_evict_first();
+    const int fill = min(p.S, nst);
+    int issued = 0, tr = 0;
+    auto relay = [&](int st) {
+      const int s = st % p.S;
+      if (!mbar_wait(full + s, (st / p.S) & 1) && lane == 0 && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
+      relay_scales<WS, P>(stages + s * L::kStageBytes, scb + s * L::kScBytes, lane, grp[0], grp[P - 1]);
+      __syncwarp();
+      mbar_arrive(ready + s);
+    };
+    for (; issued < fill; ++issued) {
+      // at most kAhead stages in flight while the ring fills: the memory system then
+      // returns this CTA's stages in order, so the first one lands early
+      if (issued >= kAhead) relay(tr++);
+      if (lane == 0) {
+        const int sl = sl0 + issued * kSPS;
+        issue_stage<WS, P>(maps, stages + (issued % p.S) * L::kStageBytes, full + issued % p.S, sl * kSliceRows,
+                           min(kSPS, sl1 - sl), ey, ex, pol);
+      }
+      __syncwarp();
+    }
+    for (; tr < nst; ++tr) {
+      relay(tr);
+      // refill: stage `issued` reuses the slot of stage issued - S, which the consumers
+      // release when they are done with it (at most one stage behind this relay)
+      while (issued < nst && issued - p.S <= tr - 1) {
+        if (lane == 0) {
+          const int old = issued - p.S;
+          if (!mbar_wait(empty + old % p.S, (old / p.S) & 1) && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
+          const int sl = sl0 + issued * kSPS;
+          issue_stage<WS, P>(maps, stages + (issued % p.S) * L::kStageBytes, full + issued % p.S, sl * kSliceRows,
+                             min(kSPS, sl1 - sl), ey, ex, pol);
         }
-        if (st >= p.S && !mbar_wait(empty + s, ((st / p.S) - 1) & 1) && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
-        const int sl = sl0 + st * kSPS;
-        issue_stage<WS, P>(maps, stages + s * L::kStageBytes, full + s, sl * kSliceRows, min(kSPS, sl1 - sl), ey, ex,
-                           pol);
+        __syncwarp();
+        ++issued;
       }
     }
-    __syncwarp();
     if (p.Ck > 1) {
       cluster_wait();
       cluster_arrive();
@@ -317,170 +357,189 @@ __global__ void __launch_bounds__((CW + 1) * 32, MINB)
 
   // ---------------- consumers ----------------
   const int g4 = lane >> 2, t4 = lane & 3;
-  const int mpart = warp % kCm, kg = warp / kCm;
-  const int mcol = mpart * 8 * MR + g4 * MR;  // first column of this thread's run in the strip
-  const int nb = mcol / 2;
-  const int ge = grp[0] + mcol / 32, go = grp[P - 1] + mcol / 32;
+  const int gl = warp % GS, kg = warp / GS;  // this warp's strip group and k group
+  // ldmatrix.x4 rows: matrix mm = lane / 8 is MMA half (mm & 1) of slice j + (mm >> 1) kKG
+  const int mm = lane >> 3;
+  const uint32_t lane_off = static_cast<uint32_t>(L::nib(L::row_of(0, 8 * (mm & 1) + (lane & 7))) +
+                                                  (mm >> 1) * kKG * L::kSliceStride + 16 * gl);
 
-  float acc[kTiles][NT][4];
+  // AS accumulator sets, one per slice in turn: 2 AS NT independent MMA chains per warp
+  // hide the tensor-pipe latency; summed in a fixed order after the loop
+  constexpr int AS = 4 / NT;
+  float acc[AS][2][NT][4];
 #pragma unroll
-  for (int i = 0; i < kTiles; ++i)
+  for (int a = 0; a < AS; ++a)
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int i = 0; i < 2; ++i)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) acc[i][nt][c] = 0.0f;
-  bool xok[NT];
-  const uint8_t* xbase[NT];
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int n = nt * 8 + g4;
-    xok[nt] = n < p.N;
-    xbase[nt] = xs + (xok[nt] ? n : 0) * kXRow;
-  }
-  // Activation slice -> shared memory [chunk][n][kXRow] in 16-byte pieces: thread t
-  // copies pieces t, t + T, t + 2T, ... of the [N][ppr] piece grid, kU loads in flight
-  // per round, (n, pc) advanced incrementally (no division in the loop).
+        for (int c = 0; c < 4; ++c) acc[a][i][nt][c] = 0.0f;
+  uint32_t xw[NT];  // this lane's activation words of the warp's first slice of chunk 0
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) xw[nt] = smem_u32(xs) + (nt * 8 + g4) * kXRow + kg * 32 + 4 * t4;
+  // Activation slice -> shared memory [chunk][n][kXRow]: item t = (batch row, k slice),
+  // 32 bytes each (for P = 2 the 16 values go even rows first, then odd rows, the
+  // order of the weight fragments); four items' loads in flight per thread. Rows N to
+  // 8 NT - 1 of the batch tiles are written as zeros, so the MMA B fragments need no
+  // per-lane predicate.
   pdl_wait();  // activations may come from the previous grid; all writes follow it
   {
-    constexpr int T = CW * 32;
-    constexpr int kU = 8;
-    const int ppr = (sl1 - sl0) * kSliceRows / 8;  // pieces per row
-    const int pieces = p.N * ppr;
-    const int k0 = sl0 * kSliceRows;
-    const int dn = T / ppr, dp = T - dn * ppr;
-    int n = threadIdx.x / ppr, pc = threadIdx.x - n * ppr;
-    for (int r0 = threadIdx.x; r0 < pieces; r0 += T * kU) {
-      uint4 v[kU];
+    constexpr int T = kCW * 32;
+    constexpr int kU = 4;
+    constexpr int kRows = NT * 8, kRowShift = NT == 1 ? 3 : (NT == 2 ? 4 : 5);
+    const int items = (sl1 - sl0) << kRowShift;
+    for (int i0 = threadIdx.x; i0 < items; i0 += T * kU) {
+      uint4 v[kU][2];
       int so[kU];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
-        v[u] = make_uint4(0u, 0u, 0u, 0u);
+        const int it = i0 + u * T;
+        v[u][0] = v[u][1] = make_uint4(0u, 0u, 0u, 0u);
         so[u] = -1;
-        if (r0 + u * T < pieces) {
-          const int k = k0 + pc * 8;
-          if (k < p.K) v[u] = __ldg(reinterpret_cast<const uint4*>(p.act + static_cast<size_t>(n) * p.K + k));
-          so[u] = (pc / (kXChunk / 8)) * p.xcstride + n * kXRow + (pc % (kXChunk / 8)) * 16;
-        }
-        pc += dp;
-        n += dn;
-        if (pc >= ppr) {
-          pc -= ppr;
-          ++n;
+        if (it < items) {
+          const int n = it & (kRows - 1), sl = it >> kRowShift;
+          const int k = (sl0 + sl) * kSliceRows;
+          const uint4* src = reinterpret_cast<const uint4*>(p.act + static_cast<size_t>(n) * p.K + k);
+          if (n < p.N && k < p.K) v[u][0] = __ldg(src);
+          if (n < p.N && k + 8 < p.K) v[u][1] = __ldg(src + 1);
+          so[u] = (sl >> 3) * p.xcstride + n * kXRow + (sl & 7) * 32;
         }
       }
 #pragma unroll
-      for (int u = 0; u < kU; ++u)
-        if (so[u] >= 0) *reinterpret_cast<uint4*>(xs + so[u]) = v[u];
+      for (int u = 0; u < kU; ++u) {
+        if (so[u] < 0) continue;
+        uint4 a = v[u][0], b = v[u][1];
+        if constexpr (P == 2) {
+          const uint4 e = make_uint4(prmt(a.x, a.y, 0x5410u), prmt(a.z, a.w, 0x5410u), prmt(b.x, b.y, 0x5410u),
+                                     prmt(b.z, b.w, 0x5410u));
+          const uint4 o = make_uint4(prmt(a.x, a.y, 0x7632u), prmt(a.z, a.w, 0x7632u), prmt(b.x, b.y, 0x7632u),
+                                     prmt(b.z, b.w, 0x7632u));
+          a = e;
+          b = o;
+        }
+        *reinterpret_cast<uint4*>(xs + so[u]) = a;
+        *reinterpret_cast<uint4*>(xs + so[u] + 16) = b;
+      }
     }
   }
-  named_bar_sync(1, CW * 32);
+  named_bar_sync(1, kCW * 32);
 
+  // per-warp bases: slot 0 of the ring, the warp's first slice; every offset inside a
+  // stage below is a compile-time constant, and the slot / parity advance incrementally
+  const NibConst kc;
+  const uint32_t wbase = smem_u32(stages) + lane_off + kg * L::kSliceStride;
+  const uint32_t scw = smem_u32(scb) + ((kg * GS + gl) * 4 + t4) * 8;
+  int s = 0;
+  uint32_t par = 0;
   for (int st = 0; st < nst; ++st) {
-    const int s = st % p.S;
-    if (!mbar_wait(full + s, (st / p.S) & 1) && lane == 0 && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
-    const uint8_t* stage = stages + s * L::kStageBytes;
+    if (!mbar_wait(ready + s, par) && lane == 0 && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
+    const uint32_t sw = wbase + s * L::kStageBytes;
+    const uint32_t scs = scw + s * L::kScBytes;
     const int n = min(kSPS, sl1 - (sl0 + st * kSPS));
-    for (int j = kg; j < n; j += kKG) {
-      const int kx = (st * kSPS + j) * kSliceRows;  // k offset within the activation slice
-      const int xo = (kx / kXChunk) * p.xcstride + (kx % kXChunk) * 2;
-      const uint8_t* xr[NT];
+    if (n == kSPS) {
+      // full stage: every ldmatrix of the warp's slices first, then the slices in turn
+      constexpr int kIt = kSPS / (2 * kKG);
+      uint32_t w[kIt][4];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) xr[nt] = xbase[nt] + xo;
-      consume_slice<NT, WS, P, MR>(stage, j * kSliceRows + 2 * t4, nb, ge, go, xr, xok, t4, acc);
+      for (int it = 0; it < kIt; ++it)
+        ldsm_x4_trans(sw + 2 * kKG * it * L::kSliceStride, w[it][0], w[it][1], w[it][2], w[it][3]);
+#pragma unroll
+      for (int it = 0; it < kIt; ++it) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int jr = (2 * it + h) * kKG;  // slice offset from the warp's first slice
+          const uint2 sc = ld_shared_v2(scs + jr * GS * 32);
+          uint32_t xr[NT];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) xr[nt] = xw[nt] + jr * 32;
+          consume_slice<NT>(kc, w[it][2 * h], w[it][2 * h + 1], xr, sc, acc[(2 * it + h) % AS]);
+        }
+      }
+    } else {
+      for (int jr = 0; kg + jr < n; jr += 2 * kKG) {
+        // lanes 16-31 address slice jr + kKG; past the stage's last slice they re-read
+        // slice jr instead (the rows stay inside the stage; the words are not used)
+        const bool hi = kg + jr + kKG < n;
+        const uint32_t back = (!hi && (lane >> 4)) ? kKG * L::kSliceStride : 0u;
+        uint32_t w0, w1, w2, w3;
+        ldsm_x4_trans(sw + jr * L::kSliceStride - back, w0, w1, w2, w3);
+        {
+          const uint2 sc = ld_shared_v2(scs + jr * GS * 32);
+          uint32_t xr[NT];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) xr[nt] = xw[nt] + jr * 32;
+          consume_slice<NT>(kc, w0, w1, xr, sc, acc[0]);
+        }
+        if (hi) {
+          const uint2 sc = ld_shared_v2(scs + (jr + kKG) * GS * 32);
+          uint32_t xr[NT];
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) xr[nt] = xw[nt] + (jr + kKG) * 32;
+          consume_slice<NT>(kc, w2, w3, xr, sc, acc[AS > 1 ? 1 : 0]);
+        }
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + s);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) xw[nt] += p.xcstride;
+    if (++s == p.S) {
+      s = 0;
+      par ^= 1u;
+    }
   }
 
-  // ---- k groups -> one partial tile per CTA ----
-  // Park the partial sums of the batch rows n < N in [kKG][N][kRow] (the ring and the
-  // activations are drained): thread (g4, t4) holds rows 8 nt + 2 t4 + (c & 1) of
-  // columns mcol + 2 i + (c >> 1).
-  named_bar_sync(1, CW * 32);
-  float* park = reinterpret_cast<float*>(smem);
-  {
-    float* rbase = park + (kg * p.N + 2 * t4) * kRow + mcol + 2 * (mcol / MR);
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+  for (int a = 1; a < AS; ++a)
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        if (nt * 8 + 2 * t4 + r < p.N) {
-          float* row = rbase + (nt * 8 + r) * kRow;
+    for (int i = 0; i < 2; ++i)
 #pragma unroll
-          for (int i = 0; i < kTiles; ++i)
-            *reinterpret_cast<float2*>(row + 2 * i) = make_float2(acc[i][nt][r], acc[i][nt][r + 2]);
-        }
-      }
-  }
-  named_bar_sync(1, CW * 32);
-  // sum the k groups in order; Ck == 1: that is the result, else it goes to the send
-  // tile, one block of N x cwp floats per owner CTA. Thread t keeps one column pair and
-  // walks the batch rows (WS / 2 divides the consumer thread count).
-  float* send = reinterpret_cast<float*>(smem + p.sendoff);
-  {
-    constexpr int kPairs = WS / 2, kDn = CW * 32 / kPairs;
-    static_assert(CW * 32 % kPairs == 0, "column pairs per pass");
-    const int col = 2 * (threadIdx.x % kPairs);
-    const int o = col / cw, lc = col - o * cw;
-    const float* src = park + col + 2 * (col / MR);
-    for (int n = threadIdx.x / kPairs; n < p.N; n += kDn) {
-      float lo = 0.0f, hi = 0.0f;
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int g = 0; g < kKG; ++g) {
-        const float2 v = *reinterpret_cast<const float2*>(src + (g * p.N + n) * kRow);
-        lo += v.x;
-        hi += v.y;
-      }
-      if (p.Ck == 1)
-        store_half2(p.out + static_cast<size_t>(n) * p.M + c0 + col, lo, hi);
-      else
-        *reinterpret_cast<float2*>(send + (o * p.N + n) * cwp + lc) = make_float2(lo, hi);
-    }
-  }
-  if (p.Ck == 1) return;
+        for (int c = 0; c < 4; ++c) acc[0][i][nt][c] += acc[a][i][nt][c];
 
-  // ---- partial tiles -> owner CTAs: one bulk copy per peer, completion on its rbar ----
-  fence_proxy_async_smem();
-  named_bar_sync(1, CW * 32);
-  cluster_wait();  // phase 0: every peer's rbar is initialised
-  const float* recv = reinterpret_cast<const float*>(smem + p.recvoff);  // [Ck][N][cwp], slot = sender
-  if (threadIdx.x == 0) {
-    for (int o = 0; o < p.Ck; ++o) {
-      if (o == q) continue;
-      bulk_copy_to_peer(mapa_shared(smem_u32(recv) + static_cast<uint32_t>(q) * blk, static_cast<uint32_t>(o)),
-                        send + o * p.N * cwp, blk, mapa_shared(smem_u32(rbar), static_cast<uint32_t>(o)));
-    }
+  // ---- partial tiles -> the owner CTA's receive slots ----
+  // owner of strip group g: CTA (g Ck) / GS of the cluster; its groups start at
+  // ceil(o GS / Ck). Slot (sender q, k group kg) holds [N][rp] floats.
+  const int own = p.owner[gl];
+  const int gfo = p.gfirst[own];
+  const int col = (gl - gfo) * 32 + 4 * g4;
+  const uint32_t slot = smem_u32(recv) + static_cast<uint32_t>((q * kKG + kg) * p.N * p.rp + col) * 4u;
+  if (p.Ck > 1) cluster_wait();  // phase 0: every CTA of the cluster runs
+  const uint32_t dst = p.Ck > 1 ? mapa_shared(slot, static_cast<uint32_t>(own)) : slot;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int n0 = nt * 8 + 2 * t4;
+    const float(&t0)[4] = acc[0][0][nt];
+    const float(&t1)[4] = acc[0][1][nt];
+    if (n0 < p.N) st_cluster_v4(dst + static_cast<uint32_t>(n0 * p.rp) * 4u, t0[0], t0[2], t1[0], t1[2]);
+    if (n0 + 1 < p.N) st_cluster_v4(dst + static_cast<uint32_t>((n0 + 1) * p.rp) * 4u, t0[1], t0[3], t1[1], t1[3]);
   }
-  if (!mbar_wait(rbar, 0) && lane == 0 && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
-  const int mine = min(cw, WS - q * cw);  // columns this CTA owns (may be <= 0)
-  if (mine > 0) {
-    // thread t: column pair i, batch row n of item t of the [N][mine / 2] grid, advanced
-    // by the thread count without a division in the loop
-    const int mp = mine / 2, T = CW * 32;
-    const int dn = T / mp, di = T - dn * mp;
-    int n = threadIdx.x / mp, i = threadIdx.x - n * mp;
-    while (n < p.N) {
-      const int lc = 2 * i;
-      float lo = 0.0f, hi = 0.0f;
-      for (int c = 0; c < p.Ck; ++c) {
-        const float* src = (c == q) ? send + (q * p.N + n) * cwp : recv + (c * p.N + n) * cwp;
-        const float2 v = *reinterpret_cast<const float2*>(src + lc);
-        lo += v.x;
-        hi += v.y;
-      }
-      store_half2(p.out + static_cast<size_t>(n) * p.M + c0 + q * cw + lc, lo, hi);
-      n += dn;
-      i += di;
-      if (i >= mp) {
-        i -= mp;
-        ++n;
-      }
-    }
+  if (p.Ck > 1) {
+    cluster_arrive();  // phase 1 (release): this CTA's partials are in their owners' slots
+    cluster_wait();
+  } else {
+    named_bar_sync(1, kCW * 32);
   }
-  // phase 1: every block addressed to this CTA has landed (a relaxed arrival: a release
-  // would first wait for this thread's output stores, which the phase does not need)
-  cluster_arrive_relaxed();
-  cluster_wait();  // phase 1: no peer still reads this CTA's send tile
+
+  // ---- owner: add the slots of its columns in (sender, k group) order ----
+  const int gf = p.gfirst[q];
+  const int c4n = (p.gfirst[q + 1] - gf) * 8;  // 4-column units this CTA owns per batch row (<= 64)
+  const int nslot = p.Ck * kKG;
+  const int c4 = threadIdx.x & 63;
+  for (int n = threadIdx.x >> 6; c4 < c4n && n < p.N; n += kCW * 32 / 64) {
+    const float* src = recv + n * p.rp + 4 * c4;
+    float4 sum = *reinterpret_cast<const float4*>(src);
+    for (int sidx = 1; sidx < nslot; ++sidx) {
+      const float4 v = *reinterpret_cast<const float4*>(src + sidx * p.N * p.rp);
+      sum.x += v.x;
+      sum.y += v.y;
+      sum.z += v.z;
+      sum.w += v.w;
+    }
+    store_half4(p.out + static_cast<size_t>(n) * p.M + c0 + gf * 32 + 4 * c4, sum.x, sum.y, sum.z, sum.w);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -528,17 +587,36 @@ __global__ void __launch_bounds__(128) k_gemm_generic(const uint16_t* __restrict
 }
 
 // ---------------------------------------------------------------------------
+// L2 prefetch companion: enqueued right before the GEMM of a call, it asks L2 for the
+// call's whole weight stream (cp.async.bulk.prefetch.L2, no shared memory, one warp
+// per CTA) so the HBM reads start while the previous kernel on the stream still holds
+// the SMs. It lets its successor (the GEMM) launch at once and finishes only after its
+// own predecessor has, so the GEMM's griddepcontrol.wait still orders it after every
+// earlier kernel of the stream.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kPrefetchPiece = 16 * 1024;
+
+__global__ void __launch_bounds__(32) k_prefetch_l2(const uint8_t* __restrict__ p, size_t bytes) {
+  pdl_launch_dependents();
+  const size_t pieces = (bytes + kPrefetchPiece - 1) / kPrefetchPiece;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * 32 + threadIdx.x; i < pieces;
+       i += static_cast<size_t>(gridDim.x) * 32) {
+    const size_t off = i * kPrefetchPiece;
+    const size_t left = bytes - off;
+    const uint32_t n = left < kPrefetchPiece ? static_cast<uint32_t>(left) : kPrefetchPiece;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + off), "r"(n & ~15u) : "memory");
+  }
+  pdl_wait();
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 struct Plan {
   int ws = 0, P = 1, Ck = 1, nt = 1, S = 0, smem = 0, ctas = 0;
-  int xchunks = 0, xcstride = 0, xbytes = 0, sendoff = 0, baroff = 0, recvoff = 0;
+  int xcstride = 0, scboff = 0, xoff = 0, recvoff = 0, baroff = 0, rp = 0;
   bool fast = false;
-  bool solo = false;  // one CTA per SM
 };
-
-static constexpr int kCW = 8;                   // consumer warps per CTA
-static constexpr int kSmemBudget = 112 * 1024;  // half an SM: room for the next call's CTA
 
 static int stage_bytes_of(int ws, int P) {
   if (ws == 256) return Layout<256, 1>::kStageBytes;
@@ -547,63 +625,45 @@ static int stage_bytes_of(int ws, int P) {
 
 static inline int round_up(int x, int a) { return (x + a - 1) / a * a; }
 
-// bytes of the k-group parking tile [kKG][N][kRow] of the final reduction
-static int park_bytes(int nt, int ws, int N) {
-  const int mr = std::min(32 / nt, ws / 8);
-  const int kg = kCW / (ws / (8 * mr));
-  const int row = (ws + 2 * ws / mr - 4 + 15) / 16 * 16 + 4;  // ParkRow<ws, mr>
-  return kg * N * row * 4;
-}
+static constexpr size_t kPrefetchMaxBytes = 42ull << 20;  // a third of the 126 MB L2
 
-// bytes of one owner block of partial sums (N rows x cwp floats), as in the kernel
-static int owner_block_bytes(int ws, int ck, int N) {
-  const int cw = ((ws + ck - 1) / ck + 1) & ~1;
-  return N * ((cw + 3) & ~3) * 4;
-}
-
-// The complete launch plan of one (strip width, cluster size) candidate: ring depth,
-// shared-memory layout and residency. pl.fast is false if it does not fit.
+// The complete launch plan of one (strip width, cluster size) candidate: ring depth and
+// shared-memory layout. pl.fast is false if it does not fit.
+//  [ring S x stage][scale pairs S x kScBytes][activations: chunks x N x 272 B]
+//  [receive slots Ck x kKG x N x rp floats][mbarriers full/empty/ready]
 static Plan make_plan(int N, int KS, int P, int ws, int ck) {
   Plan pl;
   pl.nt = N <= 8 ? 1 : (N <= 16 ? 2 : 4);
   pl.P = P;
   pl.ws = ws;
   pl.Ck = ck;
-  pl.xcstride = round_up(N * kXRow, 128);
-  const int KSc = (KS + ck - 1) / ck;
-  pl.xbytes = (KSc * kSliceRows + kXChunk - 1) / kXChunk * pl.xcstride;
-  pl.xchunks = pl.xbytes / pl.xcstride;
-  const int sb = stage_bytes_of(ws, P);
-  if (pl.xbytes + 2 * sb + 2048 > 220 * 1024) return pl;  // a large activation slice makes the CTA solo
-  const int need = (KSc + kSPS - 1) / kSPS;  // stages that hold the CTA's whole slice
-  // A CTA with a large share of the weights computes for long: one CTA per SM (at least
-  // 116 KB), since two CTAs of one call on an SM take twice as long and hold back the
-  // whole call. A small share is dominated by start-up latency: leave room for the next
-  // call's CTA to start early (programmatic dependent launch) and prefetch.
-  pl.solo = static_cast<long long>(ws) * KSc * kSliceRows >= 64 * 1024;
-  const int blk = owner_block_bytes(ws, ck, N);
-  const int recvbytes = ck > 1 ? ck * blk : 0;
-  if (pl.xbytes + 2 * sb + 2048 > kSmemBudget) pl.solo = true;
-  const int budget = pl.solo ? std::max(116 * 1024, pl.xbytes + recvbytes + 2048 + 2 * sb) : kSmemBudget;
-  int S = (budget - 2048 - pl.xbytes - recvbytes) / sb;
-  S = std::max(2, std::min(std::min(S, kMaxStages), need));
-  // the parking tile and the send tile live in the drained ring + activation region
-  pl.sendoff = round_up(park_bytes(pl.nt, ws, N), 16);
-  const int rb = pl.sendoff + (ck > 1 ? ck * blk : 0);
-  while (S * sb + pl.xbytes < rb && S < kMaxStages) ++S;
+  const int gs = ws / 32, kkg = kCW / gs;
+  const int ngmax = (gs + ck - 1) / ck;  // most groups a CTA of the cluster owns
+  pl.rp = ngmax * 32 + 4;
+  pl.xcstride = round_up(pl.nt * 8 * kXRow, 128);  // batch rows padded to the MMA tiles
+  const int KSc = (KS + ck - 1) / ck;        // most k slices a CTA of the cluster gets
+  const int need = (KSc + kSPS - 1) / kSPS;  // stages (= activation chunks) of the CTA's slice
+  const int xbytes = need * pl.xcstride;
+  const int recvbytes = ck * kkg * N * pl.rp * 4;
+  const int stage = stage_bytes_of(ws, P) + (ws / 32) * kSPS * 32;  // weights + re-laid scales
+  const int fixed = 1024 + xbytes + recvbytes + 3 * kMaxStages * 8;
+  const int want = std::min(kMaxStages, need);
+  const int S = std::min(want, (227 * 1024 - fixed) / stage);
+  // the producer's refill order needs two slots unless the CTA's slice is one stage
+  if (S < std::min(2, want) || need < 1) return pl;
   pl.S = S;
-  pl.baroff = round_up(std::max(S * sb + pl.xbytes, rb), 16);
-  pl.recvoff = pl.baroff + (2 * kMaxStages + 2) * 8;  // full, empty, rbar (+ pad)
-  pl.smem = 1024 + pl.recvoff + recvbytes;
-  if (pl.smem > 113 * 1024) pl.solo = true;  // two CTAs do not fit an SM anyway: take the registers
-  if (pl.solo) pl.smem = std::max(pl.smem, 116 * 1024);
+  pl.scboff = S * stage_bytes_of(ws, P);
+  pl.xoff = round_up(pl.scboff + S * (ws / 32) * kSPS * 32, 128);
+  pl.recvoff = round_up(pl.xoff + xbytes, 16);
+  pl.baroff = round_up(pl.recvoff + recvbytes, 16);
+  pl.smem = 1024 + pl.baroff + 3 * kMaxStages * 8;
   pl.fast = pl.smem <= 227 * 1024;
   return pl;
 }
 
-template <int NT, int WS, int P, int MINB>
+template <int NT, int WS, int P>
 static int max_clusters_q(int ck, int smem) {
-  auto kern = k_gemm_int4<NT, WS, P, kCW, MINB>;
+  auto kern = k_gemm_int4<NT, WS, P>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) {
     (void)cudaGetLastError();
     return -1;
@@ -632,35 +692,35 @@ static int max_clusters_q(int ck, int smem) {
 // SM (clusters of 7 and 8 fit only 15 times: a GPC holds two), scaled to the SM count.
 static int max_clusters(const Plan& pl, int sms) {
   int n = -1;
-  const int minb = pl.solo ? 1 : 2;
-#define MB_Q(NT_, WS_, P_)                                                                  \
-  if (pl.nt == NT_ && pl.ws == WS_ && pl.P == P_)                                           \
-    n = minb == 1 ? max_clusters_q<NT_, WS_, P_, 1>(pl.Ck, pl.smem) : max_clusters_q<NT_, WS_, P_, 2>(pl.Ck, pl.smem);
+#define MB_Q(NT_, WS_, P_) \
+  if (pl.nt == NT_ && pl.ws == WS_ && pl.P == P_) n = max_clusters_q<NT_, WS_, P_>(pl.Ck, pl.smem);
   MB_Q(1, 256, 1) MB_Q(1, 128, 1) MB_Q(1, 128, 2) MB_Q(2, 256, 1) MB_Q(2, 128, 1) MB_Q(2, 128, 2)
   MB_Q(4, 256, 1) MB_Q(4, 128, 1) MB_Q(4, 128, 2)
 #undef MB_Q
   if (n > 0) return n;
   static const int solo148[kMaxCk + 1] = {0, 148, 74, 45, 33, 26, 22, 15, 15};
-  const int base = solo148[pl.Ck] * sms / 148;
-  return pl.solo ? base : 2 * base;
+  return solo148[pl.Ck] * sms / 148;
 }
 
-// Estimated time (ns) of one call under a plan, fitted to measurements on B200:
-//  * ~3.75 us of fixed cost (launch hand-off, activation copy, first weight stage,
-//    cross-CTA reduction);
-//  * the dequant loop at ~34 / 23 / 15 weights per cycle per SM for thread runs of
-//    32 / 16 / 8 columns (MR), ~1.85 GHz under load;
+// Estimated time (ns) of one call under a plan:
+//  * a fixed cost (launch hand-off, activation copy, cross-CTA reduction);
+//  * the dequant + MMA loop at a rate per SM per cycle that falls with the batch tiles
+//    (more MMAs and activation multiplies per weight), ~1.9 GHz;
 //  * the weight stream at ~6.5 TB/s as a floor;
-//  * a cluster grid larger than the clusters the GPU holds at once runs in two waves.
+//  * a grid larger than what the GPU holds at once runs in more waves.
 static double plan_cost(const Plan& pl, int N, int K, int M, int KS, int sms) {
   const int KSc = (KS + pl.Ck - 1) / pl.Ck;
   const double w_cta = static_cast<double>(pl.ws) * KSc * kSliceRows;
-  const int mr = std::min(32 / pl.nt, pl.ws / 8);
-  const double rate = mr >= 32 ? 34.0 : (mr >= 16 ? 23.0 : 15.0);
-  double t = 3750.0 + w_cta / rate / 1.85;
+  const double rate = pl.nt == 1 ? 56.0 : (pl.nt == 2 ? 45.0 : 32.0);  // weights per cycle per SM
+  int waves = 1;
+  if (pl.Ck == 1) {
+    waves = (pl.ctas + sms - 1) / sms;
+  } else if (pl.ctas / pl.Ck > max_clusters(pl, sms)) {
+    waves = 2;
+  }
+  double t = 1500.0 + waves * w_cta / rate / 1.9;
   const double bytes = static_cast<double>(K) * M * kSB / 256 + 2.0 * N * (K + M);
-  t = std::max(t, 1500.0 + bytes / 6500.0);  // 6.5 TB/s = 6500 bytes per ns
-  if (pl.Ck > 1 && pl.ctas / pl.Ck > max_clusters(pl, sms)) t += 4000.0;
+  t = std::max(t, 800.0 + bytes / 6500.0);  // 6.5 TB/s = 6500 bytes per ns
   return t;
 }
 
@@ -670,8 +730,7 @@ static Plan plan_gemm_uncached(int N, int K, int M, int sms) {
   Plan best;
   best.nt = N <= 8 ? 1 : (N <= 16 ? 2 : 4);
   if (K % 8 != 0 || M % 128 != 0) return best;
-  const int P = (M % 256 == 0) ? 1 : ((M % 128 == 0) ? 2 : 0);
-  if (P == 0) return best;
+  const int P = (M % 256 == 0) ? 1 : 2;
   const int KS = (K + kSliceRows - 1) / kSliceRows;
   double best_t = 0.0;
   for (int ws : {256, 128}) {
@@ -773,15 +832,15 @@ static bool weight_maps(const uint8_t* sb, int K, int M, WMaps* maps) {
   return true;
 }
 
-template <int NT, int WS, int P, int MINB>
+template <int NT, int WS, int P>
 static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M,
                        uint32_t* err, cudaStream_t st) {
-  auto kern = k_gemm_int4<NT, WS, P, kCW, MINB>;
+  auto kern = k_gemm_int4<NT, WS, P>;
   static bool attr_set[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MB_ERR_LAUNCH;
   if (!attr_set[dev]) {
-    // full shared-memory carveout, so two ~112 KB CTAs (this call and the next) fit an SM
+    // full shared-memory carveout: the ring, activations and receive slots share it
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
       return MB_ERR_LAUNCH;
@@ -799,11 +858,18 @@ static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, u
   prm.KS = (K + kSliceRows - 1) / kSliceRows;
   prm.Ck = pl.Ck;
   prm.S = pl.S;
-  prm.xchunks = pl.xchunks;
   prm.xcstride = pl.xcstride;
-  prm.sendoff = pl.sendoff;
-  prm.baroff = pl.baroff;
+  prm.scboff = pl.scboff;
+  prm.xoff = pl.xoff;
   prm.recvoff = pl.recvoff;
+  prm.baroff = pl.baroff;
+  prm.rp = pl.rp;
+  for (int q = 0; q <= kMaxCk; ++q) {
+    const int qq = std::min(q, pl.Ck);
+    prm.sl_first[q] = static_cast<int>((static_cast<long long>(qq) * prm.KS) / pl.Ck);
+    prm.gfirst[q] = (qq * (WS / 32) + pl.Ck - 1) / pl.Ck;
+  }
+  for (int g = 0; g < 8; ++g) prm.owner[g] = (g * pl.Ck) / (WS / 32);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((M / WS) * pl.Ck);
@@ -823,21 +889,14 @@ static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, u
   return launch_status();
 }
 
-template <int NT, int MINB>
-static int dispatch_fast_b(const Plan& pl, const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M,
-                           uint32_t* err, cudaStream_t st) {
-  if (pl.ws == 256) return launch_fast<NT, 256, 1, MINB>(pl, act, sb, out, N, K, M, err, st);
-  if (pl.ws == 128)
-    return pl.P == 1 ? launch_fast<NT, 128, 1, MINB>(pl, act, sb, out, N, K, M, err, st)
-                     : launch_fast<NT, 128, 2, MINB>(pl, act, sb, out, N, K, M, err, st);
-  return MB_ERR_UNSUPPORTED;
-}
-
 template <int NT>
 static int dispatch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M,
                          uint32_t* err, cudaStream_t st) {
-  return pl.solo ? dispatch_fast_b<NT, 1>(pl, act, sb, out, N, K, M, err, st)
-                 : dispatch_fast_b<NT, 2>(pl, act, sb, out, N, K, M, err, st);
+  if (pl.ws == 256) return launch_fast<NT, 256, 1>(pl, act, sb, out, N, K, M, err, st);
+  if (pl.ws == 128)
+    return pl.P == 1 ? launch_fast<NT, 128, 1>(pl, act, sb, out, N, K, M, err, st)
+                     : launch_fast<NT, 128, 2>(pl, act, sb, out, N, K, M, err, st);
+  return MB_ERR_UNSUPPORTED;
 }
 
 static int launch_generic(const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M, cudaStream_t st) {
@@ -870,6 +929,14 @@ static int gemm_all(const uint16_t* act, const uint8_t* sb, uint16_t* out, int32
   if (N < 1 || K < 1 || M < 1 || (static_cast<int64_t>(K) * M) % 256 != 0) return MB_ERR_ARGS;
   if (!act || !sb || !out) return MB_ERR_NULL;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // weight streams up to a third of L2 are prefetched by the companion kernel; larger
+  // ones (an LM head) stream for long enough on their own
+  const size_t wbytes = static_cast<size_t>(K) * M / 256 * kSB;
+  if (wbytes <= kPrefetchMaxBytes && aligned(sb, 16) && wbytes >= 16) {
+    const int blocks = static_cast<int>(std::min<size_t>(sm_count(), (wbytes + 31 * kPrefetchPiece) / (32 * kPrefetchPiece)));
+    const int rc = launch_with_pdl(k_prefetch_l2, dim3(std::max(blocks, 1)), dim3(32), 0, st, sb, wbytes);
+    if (rc != MB_OK) return rc;
+  }
   for (int r0 = 0; r0 < N; r0 += 32) {
     const int nb = std::min(32, N - r0);
     const int rc = gemm_rows(act + static_cast<size_t>(r0) * K, sb, out + static_cast<size_t>(r0) * M, nb, K, M,

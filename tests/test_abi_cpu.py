@@ -56,15 +56,20 @@ def test_gemm_plans(L):
 
 
 def test_cluster_owner_ranges():
-    """The cluster kernel's final reduction gives CTA q of a Ck-CTA cluster the strip
-    columns [q cw, min((q + 1) cw, WS)) with cw = ceil(WS / Ck) rounded up to even:
-    every column has an owner rank < Ck and the ranges cover the strip exactly (the
-    planner may pick any Ck from 1 to 8)."""
-    for WS in (128, 256):
+    """The cluster kernel's final reduction gives strip group g (32 columns) to CTA
+    (g Ck) // GS of a Ck-CTA cluster, and CTA q adds the groups [ceil(q GS / Ck),
+    ceil((q + 1) GS / Ck)): every group has exactly one owner rank < Ck, the owner's
+    range contains it, the ranges tile the strip, and no CTA owns more than
+    ceil(GS / Ck) groups (the receive-slot width). The planner may pick any Ck from 1
+    to 8 for GS = 8 (256-wide strips) or 4 (128-wide)."""
+    for GS in (4, 8):
         for Ck in range(1, 9):
-            cw = ((WS + Ck - 1) // Ck + 1) & ~1
-            assert max(col // cw for col in range(0, WS, 2)) < Ck
-            assert sum(max(0, min(cw, WS - q * cw)) for q in range(Ck)) == WS
+            first = [(q * GS + Ck - 1) // Ck for q in range(Ck + 1)]
+            assert first[0] == 0 and first[-1] == GS
+            for g in range(GS):
+                own = g * Ck // GS
+                assert own < Ck and first[own] <= g < first[own + 1]
+            assert max(first[q + 1] - first[q] for q in range(Ck)) <= -(-GS // Ck)
 
 
 def test_version_and_status_strings(L):

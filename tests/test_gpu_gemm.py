@@ -1,13 +1,13 @@
 """GPU parity of the fused INT4 batched GEMM against the reference's CPU GEMM
 (golden vectors) and the NumPy oracle.
 
-Tolerance: the north-star bar is 1e-2 relative with fp32 accumulation
-(``rtol = atol = 1e-2`` as in antigravity-engine/tests/test_batched_speed.py:66-70).
-The kernel multiplies exactly the same fp16 weights (bit-exact dequant) and fp16
-activations in fp32, only the summation order differs, so it is also held to a much
-tighter bar: relative L2 error <= 1e-3 and every element within 2 fp16 ulps plus an
-absolute floor of 1e-4 x max|ref| (fp32 summation-order noise where a result
-cancels to near zero).
+Tolerance: the north-star bar, 1e-2 relative with fp32 accumulation
+(``rtol = atol = 1e-2`` as in antigravity-engine/tests/test_batched_speed.py:66-70),
+and a relative L2 error of at most 1e-3 over the whole output. The kernel sums
+``q * fp16(x * s)`` in fp32 (the group scale is applied to the activations, one fp16
+rounding per product) where the reference sums ``x * fp16(q * s)``: both carry one
+fp16 rounding per product, so results agree to about 3e-4 relative L2, not bit for
+bit. Dequantization itself is bit-exact and tested as such (test_gpu_int4.py).
 """
 
 import numpy as np
@@ -25,9 +25,6 @@ def close(got, ref):
     np.testing.assert_allclose(g, r, rtol=RTOL, atol=ATOL)
     rel = np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-30)
     assert rel <= 1e-3, f"relative L2 error {rel:.3e}"
-    ulp = np.spacing(np.abs(ref).astype(np.float16)).astype(np.float32)
-    floor = 1e-4 * float(np.max(np.abs(r))) if r.size else 0.0
-    assert np.all(np.abs(g - r) <= 2 * ulp + floor), f"max ulp err {np.max((np.abs(g - r) - floor) / ulp):.2f}"
 
 
 def run(x, st, K, M):
