@@ -9,28 +9,28 @@
 // Design (weight streaming, HBM bound):
 //  * The M columns are cut into strips of WS = 256 (one super-block per row) or 128
 //    columns. Each strip is handled by one thread-block cluster of Ck CTAs that split
-//    its K rows; the grid (strips x Ck) is one wave of the SMs.
+//    its K rows; the grid (strips x Ck) is one wave of the SMs, one CTA per SM.
 //  * One producer warp per CTA streams the CTA's super-block rows with 3-D TMA tile
 //    loads (cp.async.bulk.tensor, L2 evict-first, no multicast) into a ring of
 //    shared-memory stages guarded by mbarriers, and re-lays each landed stage's fp16
 //    group scales as (row pair, group) words for the consumers. Weights never depend on
 //    the previous kernel, so the producer starts before griddepcontrol.wait
-//    (programmatic dependent launch); a plan whose CTA fits half an SM lets the next
-//    call's CTA become resident beside this one and fill its ring while this call
-//    finishes.
-//  * Consumer warp w owns one 32-column scale group of the strip (and, for 128-wide
-//    strips, every other 16-row k slice). ldmatrix.trans of the group's nibble rows
-//    gives each lane two bytes of two consecutive k rows in one register, which a
-//    lop3 with the fp16 magic exponent turns into an mma.m16n8k16 A fragment pair
-//    (k, k+1) without any byte permute: exact integers q = n - 8. Every row of an m16
-//    tile lies in one scale group, so the group scale of row k is applied to the
-//    activations instead (B' = fp16(x[n, k] * s[k, g]), two f16x2 multiplies per 16 k
-//    rows and 8 batch rows) and the tensor core sums q * B' in fp32.
+//    (programmatic dependent launch) and the ring fills while the previous grid ends.
+//  * Each scale group (32 columns) of the strip has kKG consumer warps (16 warps per
+//    CTA). ldmatrix.trans of the group's nibble rows gives each lane two bytes of two
+//    consecutive k rows in one register, which a lop3 with the fp16 magic exponent
+//    turns into an mma.m16n8k16 A fragment pair (k, k+1) without any byte permute:
+//    exact integers q = n - 8. Every row of an m16 tile lies in one scale group, so the
+//    group scale of row k is applied to the activations instead (B' = fp16(x[n, k] *
+//    s[k, g]), two f16x2 multiplies per 16 k rows and 8 batch rows) and the tensor core
+//    sums q * B' in fp32. The kKG warps of a group take alternate stages (one batch
+//    tile) or alternate slices of every stage (more tiles, or few stages).
 //  * Reduction: every warp stores its partial tile straight into the shared memory of
 //    the cluster CTA that owns those columns (st.shared::cluster), one cluster barrier,
-//    and each owner adds the Ck x (k groups) partials of its columns in a fixed order:
+//    and each owner adds the Ck x kKG partials of its columns in a fixed order:
 //    deterministic, no global workspace, no atomics.
 #include <algorithm>
+#include <type_traits>
 #include <mutex>
 #include <unordered_map>
 
@@ -102,6 +102,8 @@ struct GemmParams {
   int sl_first[kMaxCk + 1];  // k slices [sl_first[q], sl_first[q + 1]) go to CTA q of a cluster
   int gfirst[kMaxCk + 1];    // CTA q owns strip groups [gfirst[q], gfirst[q + 1])
   int owner[8];              // the CTA that owns strip group g
+  int split;                 // 1: the kKG warps of a group take alternate stages (all 8 slices each);
+                             // 0: they take alternate slices of every stage
 };
 
 // Activations in shared memory: chunks of 128 k values (one stage) by N rows; a row
@@ -295,7 +297,7 @@ __global__ void __launch_bounds__((kCW + 1) * 32, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.S; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(empty + s, kCW);
+      mbar_init(empty + s, p.split ? GS : kCW);  // the warps that read the stage
       mbar_init(ready + s, 32);
     }
     fence_mbar_init();
@@ -359,9 +361,14 @@ __global__ void __launch_bounds__((kCW + 1) * 32, 1)
   const int g4 = lane >> 2, t4 = lane & 3;
   const int gl = warp % GS, kg = warp / GS;  // this warp's strip group and k group
   // ldmatrix.x4 rows: matrix mm = lane / 8 is MMA half (mm & 1) of slice j + (mm >> 1) kKG
+  // js: slice step between a warp's slices (1 when it takes whole stages, kKG when the
+  // group's warps share every stage); j0: its first slice of a stage
+  const bool split = p.split != 0;
+  const int js = split ? 1 : kKG, j0 = split ? 0 : kg;
+  // ldmatrix.x4 rows: matrix mm = lane / 8 is MMA half (mm & 1) of slice j + (mm >> 1) js
   const int mm = lane >> 3;
   const uint32_t lane_off = static_cast<uint32_t>(L::nib(L::row_of(0, 8 * (mm & 1) + (lane & 7))) +
-                                                  (mm >> 1) * kKG * L::kSliceStride + 16 * gl);
+                                                  (mm >> 1) * js * L::kSliceStride + 16 * gl);
 
   // AS accumulator sets, one per slice in turn: 2 AS NT independent MMA chains per warp
   // hide the tensor-pipe latency; summed in a fixed order after the loop
@@ -377,7 +384,7 @@ __global__ void __launch_bounds__((kCW + 1) * 32, 1)
         for (int c = 0; c < 4; ++c) acc[a][i][nt][c] = 0.0f;
   uint32_t xw[NT];  // this lane's activation words of the warp's first slice of chunk 0
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) xw[nt] = smem_u32(xs) + (nt * 8 + g4) * kXRow + kg * 32 + 4 * t4;
+  for (int nt = 0; nt < NT; ++nt) xw[nt] = smem_u32(xs) + (nt * 8 + g4) * kXRow + j0 * 32 + 4 * t4;
   // Activation slice -> shared memory [chunk][n][kXRow]: item t = (batch row, k slice),
   // 32 bytes each (for P = 2 the 16 values go even rows first, then odd rows, the
   // order of the weight fragments); four items' loads in flight per thread. Rows N to
@@ -428,60 +435,69 @@ __global__ void __launch_bounds__((kCW + 1) * 32, 1)
   // per-warp bases: slot 0 of the ring, the warp's first slice; every offset inside a
   // stage below is a compile-time constant, and the slot / parity advance incrementally
   const NibConst kc;
-  const uint32_t wbase = smem_u32(stages) + lane_off + kg * L::kSliceStride;
-  const uint32_t scw = smem_u32(scb) + ((kg * GS + gl) * 4 + t4) * 8;
+  const uint32_t wbase = smem_u32(stages) + lane_off + j0 * L::kSliceStride;
+  const uint32_t scw = smem_u32(scb) + ((j0 * GS + gl) * 4 + t4) * 8;
+  // a full stage, slices j0 + i * JS: every ldmatrix of the warp first, then the slices
+  auto full_stage = [&](auto jsc, uint32_t sw, uint32_t scs) {
+    constexpr int JS = decltype(jsc)::value;
+    constexpr int kIt = kSPS / (2 * JS);
+    uint32_t w[kIt][4];
+#pragma unroll
+    for (int it = 0; it < kIt; ++it)
+      ldsm_x4_trans(sw + 2 * JS * it * L::kSliceStride, w[it][0], w[it][1], w[it][2], w[it][3]);
+#pragma unroll
+    for (int it = 0; it < kIt; ++it) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int jr = (2 * it + h) * JS;  // slice offset from the warp's first slice
+        const uint2 sc = ld_shared_v2(scs + jr * GS * 32);
+        uint32_t xr[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) xr[nt] = xw[nt] + jr * 32;
+        consume_slice<NT>(kc, w[it][2 * h], w[it][2 * h + 1], xr, sc, acc[(2 * it + h) % AS]);
+      }
+    }
+  };
   int s = 0;
   uint32_t par = 0;
   for (int st = 0; st < nst; ++st) {
-    if (!mbar_wait(ready + s, par) && lane == 0 && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
-    const uint32_t sw = wbase + s * L::kStageBytes;
-    const uint32_t scs = scw + s * L::kScBytes;
-    const int n = min(kSPS, sl1 - (sl0 + st * kSPS));
-    if (n == kSPS) {
-      // full stage: every ldmatrix of the warp's slices first, then the slices in turn
-      constexpr int kIt = kSPS / (2 * kKG);
-      uint32_t w[kIt][4];
+    if (!split || (st & (kKG - 1)) == kg) {
+      if (!mbar_wait(ready + s, par) && lane == 0 && p.err) atomicOr(p.err, MB_DEVERR_TIMEOUT);
+      const uint32_t sw = wbase + s * L::kStageBytes;
+      const uint32_t scs = scw + s * L::kScBytes;
+      const int n = min(kSPS, sl1 - (sl0 + st * kSPS));
+      if (n == kSPS) {
+        if (split)
+          full_stage(std::integral_constant<int, 1>(), sw, scs);
+        else
+          full_stage(std::integral_constant<int, kKG>(), sw, scs);
+      } else {
+        for (int jr = 0; j0 + jr < n; jr += 2 * js) {
+          // lanes 16-31 address slice jr + js; past the stage's last slice they re-read
+          // slice jr instead (the rows stay inside the stage; the words are not used)
+          const bool hi = j0 + jr + js < n;
+          const uint32_t back = (!hi && (lane >> 4)) ? js * L::kSliceStride : 0u;
+          uint32_t w0, w1, w2, w3;
+          ldsm_x4_trans(sw + jr * L::kSliceStride - back, w0, w1, w2, w3);
+          {
+            const uint2 sc = ld_shared_v2(scs + jr * GS * 32);
+            uint32_t xr[NT];
 #pragma unroll
-      for (int it = 0; it < kIt; ++it)
-        ldsm_x4_trans(sw + 2 * kKG * it * L::kSliceStride, w[it][0], w[it][1], w[it][2], w[it][3]);
+            for (int nt = 0; nt < NT; ++nt) xr[nt] = xw[nt] + jr * 32;
+            consume_slice<NT>(kc, w0, w1, xr, sc, acc[0]);
+          }
+          if (hi) {
+            const uint2 sc = ld_shared_v2(scs + (jr + js) * GS * 32);
+            uint32_t xr[NT];
 #pragma unroll
-      for (int it = 0; it < kIt; ++it) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int jr = (2 * it + h) * kKG;  // slice offset from the warp's first slice
-          const uint2 sc = ld_shared_v2(scs + jr * GS * 32);
-          uint32_t xr[NT];
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) xr[nt] = xw[nt] + jr * 32;
-          consume_slice<NT>(kc, w[it][2 * h], w[it][2 * h + 1], xr, sc, acc[(2 * it + h) % AS]);
+            for (int nt = 0; nt < NT; ++nt) xr[nt] = xw[nt] + (jr + js) * 32;
+            consume_slice<NT>(kc, w2, w3, xr, sc, acc[AS > 1 ? 1 : 0]);
+          }
         }
       }
-    } else {
-      for (int jr = 0; kg + jr < n; jr += 2 * kKG) {
-        // lanes 16-31 address slice jr + kKG; past the stage's last slice they re-read
-        // slice jr instead (the rows stay inside the stage; the words are not used)
-        const bool hi = kg + jr + kKG < n;
-        const uint32_t back = (!hi && (lane >> 4)) ? kKG * L::kSliceStride : 0u;
-        uint32_t w0, w1, w2, w3;
-        ldsm_x4_trans(sw + jr * L::kSliceStride - back, w0, w1, w2, w3);
-        {
-          const uint2 sc = ld_shared_v2(scs + jr * GS * 32);
-          uint32_t xr[NT];
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) xr[nt] = xw[nt] + jr * 32;
-          consume_slice<NT>(kc, w0, w1, xr, sc, acc[0]);
-        }
-        if (hi) {
-          const uint2 sc = ld_shared_v2(scs + (jr + kKG) * GS * 32);
-          uint32_t xr[NT];
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) xr[nt] = xw[nt] + (jr + kKG) * 32;
-          consume_slice<NT>(kc, w2, w3, xr, sc, acc[AS > 1 ? 1 : 0]);
-        }
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + s);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty + s);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) xw[nt] += p.xcstride;
     if (++s == p.S) {
@@ -587,29 +603,6 @@ __global__ void __launch_bounds__(128) k_gemm_generic(const uint16_t* __restrict
 }
 
 // ---------------------------------------------------------------------------
-// L2 prefetch companion: enqueued right before the GEMM of a call, it asks L2 for the
-// call's whole weight stream (cp.async.bulk.prefetch.L2, no shared memory, one warp
-// per CTA) so the HBM reads start while the previous kernel on the stream still holds
-// the SMs. It lets its successor (the GEMM) launch at once and finishes only after its
-// own predecessor has, so the GEMM's griddepcontrol.wait still orders it after every
-// earlier kernel of the stream.
-// ---------------------------------------------------------------------------
-constexpr uint32_t kPrefetchPiece = 16 * 1024;
-
-__global__ void __launch_bounds__(32) k_prefetch_l2(const uint8_t* __restrict__ p, size_t bytes) {
-  pdl_launch_dependents();
-  const size_t pieces = (bytes + kPrefetchPiece - 1) / kPrefetchPiece;
-  for (size_t i = static_cast<size_t>(blockIdx.x) * 32 + threadIdx.x; i < pieces;
-       i += static_cast<size_t>(gridDim.x) * 32) {
-    const size_t off = i * kPrefetchPiece;
-    const size_t left = bytes - off;
-    const uint32_t n = left < kPrefetchPiece ? static_cast<uint32_t>(left) : kPrefetchPiece;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + off), "r"(n & ~15u) : "memory");
-  }
-  pdl_wait();
-}
-
-// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 struct Plan {
@@ -624,8 +617,6 @@ static int stage_bytes_of(int ws, int P) {
 }
 
 static inline int round_up(int x, int a) { return (x + a - 1) / a * a; }
-
-static constexpr size_t kPrefetchMaxBytes = 42ull << 20;  // a third of the 126 MB L2
 
 // The complete launch plan of one (strip width, cluster size) candidate: ring depth and
 // shared-memory layout. pl.fast is false if it does not fit.
@@ -870,6 +861,11 @@ static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, u
     prm.gfirst[q] = (qq * (WS / 32) + pl.Ck - 1) / pl.Ck;
   }
   for (int g = 0; g < 8; ++g) prm.owner[g] = (g * pl.Ck) / (WS / 32);
+  // whole stages per warp for one batch tile when every warp of a group gets at least
+  // two of them (measured: faster at N <= 8, slower with more batch tiles)
+  const int kkg = kCW / (WS / 32);
+  const int need = ((prm.KS + pl.Ck - 1) / pl.Ck + kSPS - 1) / kSPS;
+  prm.split = (NT == 1 && need >= 2 * kkg) ? 1 : 0;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((M / WS) * pl.Ck);
@@ -929,14 +925,6 @@ static int gemm_all(const uint16_t* act, const uint8_t* sb, uint16_t* out, int32
   if (N < 1 || K < 1 || M < 1 || (static_cast<int64_t>(K) * M) % 256 != 0) return MB_ERR_ARGS;
   if (!act || !sb || !out) return MB_ERR_NULL;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // weight streams up to a third of L2 are prefetched by the companion kernel; larger
-  // ones (an LM head) stream for long enough on their own
-  const size_t wbytes = static_cast<size_t>(K) * M / 256 * kSB;
-  if (wbytes <= kPrefetchMaxBytes && aligned(sb, 16) && wbytes >= 16) {
-    const int blocks = static_cast<int>(std::min<size_t>(sm_count(), (wbytes + 31 * kPrefetchPiece) / (32 * kPrefetchPiece)));
-    const int rc = launch_with_pdl(k_prefetch_l2, dim3(std::max(blocks, 1)), dim3(32), 0, st, sb, wbytes);
-    if (rc != MB_OK) return rc;
-  }
   for (int r0 = 0; r0 < N; r0 += 32) {
     const int nb = std::min(32, N - r0);
     const int rc = gemm_rows(act + static_cast<size_t>(r0) * K, sb, out + static_cast<size_t>(r0) * M, nb, K, M,
