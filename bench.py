@@ -33,6 +33,8 @@ import subprocess
 import sys
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -118,6 +120,23 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # reference arm / CPU baseline: the oracle port of the reference's CPU path
 # ---------------------------------------------------------------------------
+def all_cores() -> int:
+    """Raise the NumPy BLAS / OpenMP and torch thread limits to every host core
+    (torchrun starts its workers with OMP_NUM_THREADS=1) and return the core count."""
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=n)
+    except Exception:
+        pass
+    try:
+        import torch
+        torch.set_num_threads(n)
+    except Exception:
+        pass
+    return n
+
+
 class CpuReference:
     """The reference's CPU path per call: ``unpack_superblock_weights`` (src/dequant.py:116-147)
     then the fp32 NumPy GEMM (test_batched_speed.py:39-42), via the oracle port.
@@ -125,6 +144,7 @@ class CpuReference:
 
     def __init__(self):
         from oracle import int4 as O
+        all_cores()
         self.O = O
         self.st = O.quantize_pack_matrix(O.make_weights(K_DIM, M_DIM, SEED))
         self.xs = {n: O.make_activations(n, K_DIM, n) for n in SWEEP}
@@ -343,7 +363,8 @@ def run_moat(args):
             tr = sum(per[str(n)] for n in sweep) / len(sweep)
 
     attn = None if (world > 1 or args.no_attn) else attention_side(dev, peak, peak_kind, with_cpu=not args.no_cpu)
-    decode = None if args.no_decode else decode_side(dev, rank, world)
+    cfg2 = None if (world > 1 or args.no_config2) else config2_side(dev, peak, peak_kind)
+    decode = None if args.no_decode else decode_side(dev, rank, world, with_cpu=not args.no_cpu)
     sampling = None if (world > 1 or args.no_decode) else sampling_side(dev)
 
     if rank == 0:
@@ -370,6 +391,7 @@ def run_moat(args):
             "e2e": e2e,
             "cpu_baseline": cpu,
             "attention": attn,
+            "config2": cfg2,
             "decode": decode,
             "sampling": sampling,
         }
@@ -378,6 +400,62 @@ def run_moat(args):
         graphs.clear()
         dist.destroy_process_group()
     return 0
+
+
+def config2_side(dev, peak, peak_kind, reps: int = 5):
+    """BASELINE config 2 (Qwen-1.5B-like FFN up-projection, INT4 K=2048 x M=5504,
+    N = 1, 2, 4, 8, 16, 32, one GPU): per N the GEMM over a ring of weight copies far
+    larger than L2, replayed from a CUDA graph, CUDA-event timed; us per call, achieved
+    GB/s and the fraction of the measured HBM peak. Reported beside the config-3 line."""
+    import torch
+    from moat_b200 import _lib
+    from moat_b200.dequant import quantize_to_superblocks
+    from moat_b200.gemm import plan
+    L = _lib.lib()
+    K, M = 2048, 5504
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 2)
+    sb = quantize_to_superblocks((torch.randn((K, M), generator=g, device=dev) * 0.02).reshape(-1))
+    R = -(-4 * L2_BYTES // sb.numel())
+    ring = torch.empty((R, sb.numel()), dtype=torch.uint8, device=dev)
+    ring[:] = sb
+    st = torch.cuda.Stream(device=dev)
+    out = {}
+    for n in SWEEP:
+        x = torch.randn((n, K), generator=g, device=dev).half()
+        y = torch.empty((R, n, M), dtype=torch.float16, device=dev)
+
+        def launches():
+            for r in range(R):
+                rc = L.mb_int4_gemm(x.data_ptr(), ring[r].data_ptr(), y[r].data_ptr(), n, K, M, None, st.cuda_stream)
+                if rc != 0:
+                    raise RuntimeError(f"mb_int4_gemm failed: {rc}")
+
+        with torch.cuda.stream(st):
+            launches()
+            st.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=st):
+                launches()
+            for _ in range(3):
+                gr.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(reps):
+                gr.replay()
+            e1.record(st)
+            st.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * R)
+        b = gemm_bytes(n, K, M)
+        out[str(n)] = {"us_per_call": us, "GBps": b / us / 1e3, "frac": b / us / 1e3 / peak,
+                       "tok_per_s": n / us * 1e6, "plan": plan(n, K, M)}
+        del gr, y
+    del ring
+    torch.cuda.empty_cache()
+    return {"workload": "BASELINE config 2: INT4 super-block GEMM K=2048 x M=5504, N sweep "
+                        + ",".join(map(str, SWEEP)) + ", one GPU",
+            "ring_copies": R, "l2": "inputs larger than L2 (weight ring)", "peak": peak, "peak_kind": peak_kind,
+            "per_n": out}
 
 
 def attention_side(dev, peak, peak_kind, reps: int = 10, with_cpu: bool = True):
@@ -436,6 +514,7 @@ def attention_cpu_baseline(T, H, Lk, d, budget_s: float = 6.0):
     sample until the budget is spent."""
     from oracle import attention as OA
     from moat_b200.attention import attention_bytes
+    cores = all_cores()
     q, k, v = OA.make_attention_inputs(T, H, Lk, d, SEED + 11)
     tbl = OA.exp_table(32768, 16.0)
     calls, t0 = 0, time.perf_counter()
@@ -445,32 +524,52 @@ def attention_cpu_baseline(T, H, Lk, d, budget_s: float = 6.0):
         el = time.perf_counter() - t0
         if el >= budget_s or calls >= 20:
             break
-    return {"value": attention_bytes(T, H, Lk, d) * calls / el / 1e9, "unit": "GB/s", "cores": os.cpu_count(),
+    return {"value": attention_bytes(T, H, Lk, d) * calls / el / 1e9, "unit": "GB/s", "cores": cores,
             "kind": "port", "sample": f"{calls} full config-4 calls ({el:.1f} s) of the NumPy composition "
                                        "(einsum scores, LUT softmax, einsum with V)",
             "us_per_call": el / calls * 1e6}
 
 
-def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 64):
-    """BASELINE config 5 decode speed: a random-init Qwen-1.5B-like INT4 decoder (24
-    layers, hidden 2048, 16 heads x 128, FFN 5504, vocab 151936), N = 16 traces, the
-    KV cache seeded for a 512-token prompt, greedy steps replayed from one captured
-    CUDA graph and timed with CUDA events (maximum over ranks). With ``world`` > 1 the
-    decoder is tensor-parallel: heads, FFN and vocabulary split over the ranks, two
-    exchanges per layer (each rank stores its partial rows into the others' buffers over
-    NVLink; one kernel joins them with the residual add and RMSNorm) and one for the
-    greedy choice, all inside the graph; tokens/s counts the N tokens the whole job
-    makes per step (total work fixed: strong scaling). Reported beside the GEMM line."""
+def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 256, prompt: int = 512, check_steps: int = 16,
+                with_cpu: bool = True):
+    """BASELINE config 5 as written: a random-init Qwen-1.5B-like INT4 decoder (24
+    layers, hidden 2048, 16 heads x 128, FFN 5504, vocab 151936), N = 16 traces, a
+    prompt of 512 seeded random token ids run through the decode step one position at
+    a time (the reference engine's prefill loop), then 256 greedy steps replayed from one
+    captured CUDA graph and timed with CUDA events (maximum over ranks). With ``world``
+    > 1 the decoder is tensor-parallel: heads, FFN and vocabulary split over the ranks,
+    two exchanges per layer (peer stores over NVLink, one kernel that joins the partial
+    rows with the residual add and RMSNorm) and one for the greedy choice, all inside
+    the graph; tokens/s counts the N tokens the whole job makes per step (total work
+    fixed: strong scaling).
+
+    Then the decoder is rewound to the end of the prompt and ``check_steps`` greedy
+    steps are replayed eagerly, recording each step's input and output ids. On one GPU
+    the reference-style CPU forward (oracle port of transformer.py:161-225 with the same
+    dequantized weights, fp32, every host core) replays the same inputs from the same
+    cache: its time is the decode CPU baseline and its argmax agreement with the GPU's
+    ids is reported (exact softmax, the reference's TinyLlamaModel; exp-LUT softmax, the
+    reference's batch decode path). On N GPUs every rank also builds the whole model as
+    a replica and replays the tensor-parallel inputs: the number of differing ids is
+    reported. Reported beside the GEMM line."""
     import torch
     from moat_b200.decode import DecoderConfig, Int4Decoder, timed_decode
-    cfg = DecoderConfig()
-    N, P = 16, 512
+    cfg = DecoderConfig(max_len=prompt + steps + 16)
+    N = 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 6)
+    prompt_ids = torch.randint(0, cfg.vocab, (N, prompt), generator=g, device=dev, dtype=torch.int32)
     dec = Int4Decoder(cfg, N, device=dev, seed=SEED + 5, rank=rank, world=world, exchange_timeout_s=2.0)
+    cpu = None
+    tp_check = None
     try:
-        dec.fill_prompt_cache(P, seed=SEED + 6)
-        g = torch.Generator(device=dev)
-        g.manual_seed(SEED + 7)
-        dec.ids.copy_(torch.randint(0, cfg.vocab, (N,), generator=g, device=dev, dtype=torch.int32))
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        dec.prefill(prompt_ids)
+        torch.cuda.synchronize()
+        prefill_s = time.perf_counter() - t0
+        snap = dec.cache_snapshot()
+        first = dec.ids.clone()
         try:
             ms = timed_decode(dec, steps, warmup=3, graph=True)
         except RuntimeError as e:  # raised on every rank alike (the check is all-reduced)
@@ -478,12 +577,22 @@ def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 64):
         err = int(dec.err.item())
         wbytes = sum(sum(int(lw[k].numel()) for k in ("wqkv", "wo", "wgu", "wd")) for lw in dec.layers) \
             + int(dec.lm_head.numel())
-        kv = 2 * cfg.layers * N * dec.Hl * cfg.head_dim * 2 * (P + 5 + steps // 2)  # mean cache length
+        kv = 2 * cfg.layers * N * dec.Hl * cfg.head_dim * 2 * (prompt + 5 + steps // 2)  # mean cache length
         tot = torch.tensor([float(wbytes + kv), float(err)], dtype=torch.float64, device=dev)
         if world > 1:
             import torch.distributed as dist
             dist.all_reduce(tot)
         step_bytes, err = float(tot[0].item()), int(tot[1].item())
+        # rewind to the end of the prompt and record a short greedy trajectory
+        dec.restore_cache(snap)
+        ids = first.clone()
+        ins, outs = [], []
+        for _ in range(check_steps):
+            ins.append(ids.cpu())
+            ids = dec.step(ids).clone()
+            outs.append(ids.cpu())
+        if world == 1 and with_cpu and rank == 0:
+            cpu = decode_cpu_baseline(dec, snap, ins, outs)
     finally:
         dec.close()  # graph and exchange buffers go before the process group
     del dec
@@ -493,26 +602,73 @@ def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 64):
         import torch.distributed as dist
         rep = Int4Decoder(cfg, N, device=dev, seed=SEED + 5)
         try:
-            rep.fill_prompt_cache(P, seed=SEED + 6)
-            rep.ids.copy_(torch.randint(0, cfg.vocab, (N,), generator=g, device=dev, dtype=torch.int32))
+            rep.prefill(prompt_ids)
+            rsnap = rep.cache_snapshot()
+            rfirst = rep.ids.clone()
+            # the replica replays the tensor-parallel decoder's inputs from its own cache
+            bad = 0
+            for i, o in zip(ins, outs):
+                bad += int((rep.step(i.to(dev)).cpu() != o).sum().item())
+            bad += int((rfirst.cpu() != ins[0]).sum().item())
+            rep.restore_cache(rsnap)
+            rep.ids.copy_(rfirst)
             rms = timed_decode(rep, steps, warmup=3, graph=True)
         finally:
             rep.close()
-        m = torch.tensor([rms], dtype=torch.float64, device=dev)
+        m = torch.tensor([rms, float(bad)], dtype=torch.float64, device=dev)
         dist.all_reduce(m, op=dist.ReduceOp.MAX)
-        rms = float(m.item())
+        rms, bad = float(m[0].item()), int(m[1].item())
         replicas = {"tok_per_s": world * N / rms * 1e3, "ms_per_step": rms, "traces_per_gpu": N,
                     "scaling": "weak", "note": "independent full-model replicas, no collective; max over ranks"}
+        tp_check = {"tp_vs_replica_mismatch": bad, "ids_compared": N * (check_steps + 1),
+                    "how": "the one-GPU replica replays the tensor-parallel decoder's greedy inputs from its own "
+                           "prefilled cache (first token + %d steps); max over ranks" % check_steps}
         del rep
         torch.cuda.empty_cache()
     return {"workload": "BASELINE config 5: 24-layer INT4 decoder, hidden 2048, 16x128 heads, FFN 5504, "
-                        "vocab 151936; 16 traces, 512-position cache, greedy", "metric": "decode tok/s",
-            "tok_per_s": N / ms * 1e3, "ms_per_step": ms, "steps": steps, "graph": True,
+                        "vocab 151936; 16 traces, 512-token random prompt run through the step, 256 greedy steps",
+            "metric": "decode tok/s", "tok_per_s": N / ms * 1e3, "ms_per_step": ms, "steps": steps,
+            "prompt": prompt, "prefill_s": prefill_s, "prefill_tok_per_s": N * prompt / prefill_s, "graph": True,
             "tensor_parallel": world, "scaling": "strong" if world > 1 else None,
             "exchange": "NVLink peer stores (mb_peer_add_rmsnorm, mb_peer_argmax)" if world > 1 else None,
             "bytes_per_step": step_bytes, "GBps": step_bytes / ms / 1e6, "device_error_bits": err,
-            "replicas": replicas,
-            "data": "synthetic (random-init weights quantized to INT4; KV cache seeded N(0,1))"}
+            "replicas": replicas, "tp_check": tp_check, "cpu_baseline": cpu,
+            "data": "synthetic (random-init weights quantized to INT4; seeded random prompt ids)"}
+
+
+def decode_cpu_baseline(dec, snap, ins, outs):
+    """The reference-style CPU decoder forward (oracle port of transformer.py:161-225:
+    fp32 torch on every host core, the GPU decoder's INT4 weights dequantized) replays
+    the GPU's recorded greedy inputs from the prompt's cache; timed with the exact
+    softmax (the reference's TinyLlamaModel), then run again with the exp-LUT softmax of
+    the reference's batch decode path. Reports tok/s and both argmax agreements."""
+    import torch
+    from oracle.decoder import CpuDecoder, argmax_agreement
+    threads = all_cores()
+    cfg = dec.cfg
+    dense = dec.dense_weights()
+    ks, vs, n = snap
+    gpu = np.stack([o.numpy() for o in outs])
+    res = {}
+    for mode in ("exact", "lut"):
+        cpu = CpuDecoder(dense["layers"], dense["final_norm"], dense["lm_head"], dense["embed"], dense["cis"],
+                         cfg.heads, dec.N, n + len(ins) + 1, eps=cfg.eps, softmax=mode, lut=dec.lut.lut,
+                         lut_range=cfg.lut_range)
+        cpu.load_cache(ks, vs, n)
+        got = []
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            for i in ins:
+                got.append(torch.argmax(cpu.step(i), dim=-1).numpy())
+        res[mode] = (argmax_agreement(np.stack(got), gpu), time.perf_counter() - t0)
+        del cpu
+    el = res["exact"][1]
+    return {"value": dec.N * len(ins) / el, "unit": "tok/s", "cores": threads, "kind": "port",
+            "ms_per_step": el / len(ins) * 1e3,
+            "sample": f"{len(ins)} greedy steps of 16 traces from the 512-token prompt's cache, fp32 torch CPU "
+                      "forward (transformer.py semantics, exact softmax) with the dequantized INT4 weights",
+            "argmax_agreement_exact_softmax": res["exact"][0], "argmax_agreement_lut_softmax": res["lut"][0],
+            "ids_compared": int(gpu.size)}
 
 
 def sampling_side(dev, calls: int = 50):
@@ -606,6 +762,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-attn", action="store_true", help="skip the config-4 attention side measurement")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-5 decode side measurement")
+    ap.add_argument("--no-config2", action="store_true", help="skip the config-2 (2048 x 5504) sweep")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--e2e-ring", type=int, default=36)
     ap.add_argument("--e2e-steps", type=int, default=3)

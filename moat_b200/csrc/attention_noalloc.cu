@@ -15,7 +15,7 @@
 //   - Limit: MB_ATTN_NOALLOC_SCRATCH_BYTES (16 MiB) per device. A shape whose
 //     mb_decode_attn_workspace_size() is larger is rejected with MB_ERR_WORKSPACE and
 //     nothing is launched (16 traces x 16 heads x 4096 positions x d = 128 needs
-//     about 6.3 MB).
+//     5,254,400 bytes, about 5.3 MB).
 //   - Nothing in the scratch has to start at zero: pass 1 rewrites the per-row
 //     arrival counters before pass 3 counts on them, and every other scratch byte is
 //     written before it is read.

@@ -212,6 +212,68 @@ class Int4Decoder:
         self.length = length
         self.pos.fill_(length)
 
+    def prefill(self, prompt_ids):
+        """Run a prompt through the decoder one position at a time, as the reference's
+        engine does (``transformer_engine.mm:846-881``: every prompt token goes through
+        the decode step, its keys and values land in the cache, and the last position's
+        logits give the first generated token). ``prompt_ids``: int32 ``[N, P]`` on the
+        device. The first position runs eagerly (it caches GEMM plans and tensor maps),
+        the rest replay the captured step with the prompt token copied into
+        ``self.ids`` before each replay. Leaves the first generated ids in ``self.ids``
+        and ``P`` positions in the cache."""
+        t = _lib.torch()
+        if prompt_ids.dim() != 2 or prompt_ids.shape[0] != self.N:
+            raise ValueError(f"prompt ids must be [{self.N}, P]")
+        P = int(prompt_ids.shape[1])
+        if self.length + P >= self.cfg.max_len:
+            raise ValueError("prompt does not fit the KV cache")
+        ids = prompt_ids.to(device=self.dev, dtype=t.int32)
+        for p in range(P):
+            if p == 0:
+                self.step(ids[:, 0].contiguous())
+                self.capture()
+                continue
+            self.ids.copy_(ids[:, p])
+            self.step_graphed()
+        return self.ids
+
+    def cache_snapshot(self, length=None):
+        """Host copies of the first ``length`` cached positions of every layer (keys,
+        values), to rewind the decoder with ``restore_cache``."""
+        n = self.length if length is None else length
+        return ([k[:, :, :n].cpu() for k in self.k_cache], [v[:, :, :n].cpu() for v in self.v_cache], n)
+
+    def restore_cache(self, snap):
+        """Rewind to a ``cache_snapshot``: its positions are written back, the next
+        position is its length on the host and on the device."""
+        ks, vs, n = snap
+        for dst, src in zip(self.k_cache, ks):
+            dst[:, :, :n].copy_(src)
+        for dst, src in zip(self.v_cache, vs):
+            dst[:, :, :n].copy_(src)
+        self.length = n
+        self.pos.fill_(n)
+
+    def dense_weights(self):
+        """The model with every INT4 stream dequantized (bit-exact fp16 values, as fp32
+        CPU tensors ``[K, M]``) and the fp32 norms, embedding and RoPE factors on the
+        host: the inputs of a reference-style CPU forward. One GPU only."""
+        t = _lib.torch()
+        from .dequant import unpack_superblock_weights
+        if self.world != 1:
+            raise ValueError("dense_weights needs the whole model (world = 1)")
+        cfg = self.cfg
+        D, F, V = cfg.hidden, cfg.ffn, cfg.vocab
+
+        def deq(sb, K, M):
+            return unpack_superblock_weights(sb, K * M // 256).reshape(K, M).float().cpu()
+
+        layers = [{"wqkv": deq(lw["wqkv"], D, 3 * D), "wo": deq(lw["wo"], D, D), "wgu": deq(lw["wgu"], D, 2 * F),
+                   "wd": deq(lw["wd"], F, D), "attn_norm": lw["attn_norm"].cpu(), "ffn_norm": lw["ffn_norm"].cpu()}
+                  for lw in self.layers]
+        return {"layers": layers, "final_norm": self.final_norm.cpu(), "lm_head": deq(self.lm_head, D, V),
+                "embed": self.embed.float().cpu(), "cis": t.view_as_complex(self.cs.cpu().contiguous())}
+
     def step(self, ids):
         """One decode step for all traces: token ids [N] (int32, device) in, the next
         ids [N] out (a device tensor, also kept in ``self.ids``)."""

@@ -127,6 +127,34 @@ def test_argmax_ties_and_nan(cuda):
     assert ids.cpu().numpy().tolist()[1:] == [100, 77, 0]
 
 
+def test_argmax_odd_width_unaligned_rows_and_tail(cuda):
+    """V = 1001: rows after the first start off a 16-byte boundary (the scalar row
+    scan) and the first row ends in a one-column tail after its 16-byte loads. A tie, a
+    NaN, a -0 / +0 pair and the row maximum are placed in those tail columns and
+    unaligned rows; mb_argmax_f16 equals numpy.argmax and mb_argmax_key_f16 the
+    oracle's keys (column offset 4096)."""
+    import torch
+    from oracle import sampling as S
+    L = _lib()
+    N, V, col0 = 4, 1001, 4096
+    g = torch.Generator(device=cuda).manual_seed(5)
+    x = torch.randn((N, V), generator=g, device=cuda).half()
+    x[0, 1000] = 9.0                      # the maximum in the tail column of the aligned row
+    x[1, 3] = x[1, 1000] = 7.5            # tie in an unaligned row: the first index wins
+    x[2, 999] = float("nan")              # NaN near the end of an unaligned row
+    x[3, :] = -1.0
+    x[3, 997] = -0.0
+    x[3, 1000] = 0.0                      # -0 == +0: the first of them wins
+    ids = torch.empty(N, dtype=torch.int32, device=cuda)
+    keys = torch.zeros(N, dtype=torch.int64, device=cuda)
+    assert L.mb_argmax_f16(x.data_ptr(), N, V, ids.data_ptr(), _st()) == 0
+    assert L.mb_argmax_key_f16(x.data_ptr(), N, V, col0, keys.data_ptr(), _st()) == 0
+    torch.cuda.synchronize()
+    xn = x.cpu().numpy()
+    assert ids.cpu().numpy().tolist() == S.reference_argmax(xn).tolist() == [1000, 3, 999, 997]
+    np.testing.assert_array_equal(keys.cpu().numpy(), S.argmax_keys(xn, col0))
+
+
 @pytest.mark.parametrize("L_used,Lmax,d", [(1, 32, 128), (300, 768, 128), (513, 600, 64)])
 def test_attention_over_cache(cuda, L_used, Lmax, d):
     import torch
@@ -256,3 +284,45 @@ def test_sampled_decode_step_matches_oracle_draw(cuda):
         assert dec.ids.cpu().numpy().tolist() == otok.tolist()
         np.testing.assert_allclose(dec.logprobs.cpu().numpy(), olp, rtol=1e-6, atol=1e-6)
     assert int(dec.err.item()) == 0
+
+
+def test_config5_full_shape_greedy_agreement(cuda):
+    """BASELINE config 5 at full shape (24 layers, hidden 2048, 16 x 128 heads, FFN 5504,
+    vocabulary 151,936, N = 16): a 32-token random prompt runs through the step, then
+    16 greedy steps; the reference-style CPU forward (``oracle/decoder.py``, fp32 torch,
+    the same dequantized weights, the prompt's cache copied from the GPU) replays the
+    GPU's inputs. The north-star bar is argmax agreement >= 99% over the 256 (trace,
+    step) ids, against the reference's exp-LUT decode softmax (batch_generator.py:226)
+    and against its exact-softmax TinyLlamaModel (transformer.py:117)."""
+    import os
+    import torch
+    from moat_b200.decode import DecoderConfig, Int4Decoder
+    from oracle.decoder import CpuDecoder, argmax_agreement
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = DecoderConfig(max_len=64)
+    N, P, S = 16, 32, 16
+    dec = Int4Decoder(cfg, N, device=cuda, seed=21)
+    try:
+        g = torch.Generator(device=cuda).manual_seed(22)
+        dec.prefill(torch.randint(0, cfg.vocab, (N, P), generator=g, device=cuda, dtype=torch.int32))
+        snap = dec.cache_snapshot()
+        ids = dec.ids.clone()
+        ins, outs = [], []
+        for _ in range(S):
+            ins.append(ids.cpu())
+            ids = dec.step(ids).clone()
+            outs.append(ids.cpu().numpy())
+        assert int(dec.err.item()) == 0
+        dense = dec.dense_weights()
+    finally:
+        dec.close()
+    gpu = np.stack(outs)
+    for mode in ("lut", "exact"):
+        cpu = CpuDecoder(dense["layers"], dense["final_norm"], dense["lm_head"], dense["embed"], dense["cis"],
+                         cfg.heads, N, P + S + 1, eps=cfg.eps, softmax=mode, lut=dec.lut.lut, lut_range=cfg.lut_range)
+        cpu.load_cache(snap[0], snap[1], snap[2])
+        with torch.no_grad():
+            got = np.stack([torch.argmax(cpu.step(i), dim=-1).numpy() for i in ins])
+        agree = argmax_agreement(got, gpu)
+        assert agree >= 0.99, (mode, agree)
+        del cpu

@@ -2,8 +2,9 @@
 
 It runs the same kernels as ``mb_decode_attn`` on a scratch array owned by the
 library, so on the same inputs its output must match the workspace entry point.
-Two calls in a row with different shapes check that what the first call leaves in
-the scratch does not leak into the second. This file sorts last so the test also
+Two calls in a row with different shapes, both on the three-pass path that uses the
+scratch, check that what the first call leaves in the scratch (statistics, arrival
+counters) does not leak into the second. This file sorts last so the test also
 runs after every other GPU test has used the device.
 """
 
@@ -45,9 +46,11 @@ def test_noalloc_matches_workspace_entry_point(L, cuda):
     table = lut.device_table(cuda)
     st = torch.cuda.current_stream(cuda).cuda_stream
     rng = np.random.default_rng(11)
-    # two calls in a row: config 4 (16 traces x 16 heads x 4096 x 128), then a
-    # smaller ragged shape, so the second call runs on what the first left behind
-    for T, H, Lk, d in ((16, 16, 4096, 128), (3, 5, 777, 64)):
+    # two calls in a row, both on the three-pass path (caches longer than the
+    # 2048-position one-CTA-per-row path): config 4 (16 traces x 16 heads x 4096 x 128),
+    # then a ragged shape with other row and chunk counts, so the second call's
+    # statistics and arrival counters start from what the first call left in the scratch
+    for T, H, Lk, d in ((16, 16, 4096, 128), (3, 5, 2600, 64)):
         q = torch.from_numpy(rng.standard_normal((T, H, d)).astype(np.float16)).to(cuda)
         k = torch.from_numpy(rng.standard_normal((T, H, Lk, d)).astype(np.float16)).to(cuda)
         v = torch.from_numpy(rng.standard_normal((T, H, Lk, d)).astype(np.float16)).to(cuda)
