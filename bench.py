@@ -362,10 +362,11 @@ def run_moat(args):
         if all(str(n) in per for n in sweep) and world == 1:
             tr = sum(per[str(n)] for n in sweep) / len(sweep)
 
-    attn = None if (world > 1 or args.no_attn) else attention_side(dev, peak, peak_kind, with_cpu=not args.no_cpu)
+    attn = None if args.no_attn else attention_side(dev, peak, peak_kind, with_cpu=not args.no_cpu, rank=rank,
+                                                    world=world)
     cfg2 = None if (world > 1 or args.no_config2) else config2_side(dev, peak, peak_kind)
     decode = None if args.no_decode else decode_side(dev, rank, world, with_cpu=not args.no_cpu)
-    sampling = None if (world > 1 or args.no_decode) else sampling_side(dev)
+    sampling = None if (world > 1 or args.no_decode) else sampling_side(dev, rows=(16,))
 
     if rank == 0:
         cpu = None if (world > 1 or args.no_cpu) else cpu_reference(budget_s=args.cpu_seconds)
@@ -458,39 +459,53 @@ def config2_side(dev, peak, peak_kind, reps: int = 5):
             "per_n": out}
 
 
-def attention_side(dev, peak, peak_kind, reps: int = 10, with_cpu: bool = True):
+def attention_side(dev, peak, peak_kind, reps: int = 10, with_cpu: bool = True, rank: int = 0, world: int = 1):
     """BASELINE config 4 decode attention (16 traces x 16 heads, KV length 4096, d 128,
-    fp16 KV, 32,768-entry LUT over [-16, 0]) timed on its own with CUDA events: two KV
-    copies alternate so each call streams from HBM (2 x 537 MB > L2). Reported beside
-    the GEMM line, not part of its value."""
+    fp16 KV, 32,768-entry LUT over [-16, 0]) timed with CUDA events, the KV copies
+    rotated so each call streams from HBM (together far larger than L2). With ``world``
+    > 1 the heads are sharded (rank r computes its head range) and every call ends with
+    the NCCL all-gather of the [16, 16, 128] output; the time is the maximum over ranks
+    and GB/s counts every head's K and V. Reported beside the GEMM line, not part of
+    its value."""
     import torch
     from moat_b200 import _lib
     from moat_b200.attention import ExponentialLUT, attention_bytes
+    from moat_b200.dist import gather_heads, head_bounds
     L = _lib.lib()
     T, H, Lk, d = 16, 16, 4096, 128
+    bounds = head_bounds(H, world)
+    h0, h1 = bounds[rank]
+    Hl = h1 - h0
     g = torch.Generator(device=dev)
     g.manual_seed(SEED + 7)
-    q = torch.randn((T, H, d), generator=g, device=dev).half()
-    kv = [(torch.randn((T, H, Lk, d), generator=g, device=dev).half(),
-           torch.randn((T, H, Lk, d), generator=g, device=dev).half()) for _ in range(2)]
+    q = torch.randn((T, H, d), generator=g, device=dev).half()[:, h0:h1].contiguous()
+    copy_bytes = 2 * T * Hl * Lk * d * 2
+    copies = max(2, -(-4 * L2_BYTES // copy_bytes))
+    kv = [(torch.randn((T, Hl, Lk, d), generator=g, device=dev).half(),
+           torch.randn((T, Hl, Lk, d), generator=g, device=dev).half()) for _ in range(copies)]
     lut = ExponentialLUT(range_max=16.0)
     tab = lut.device_table(dev)
-    out = torch.empty((T, H, d), dtype=torch.float16, device=dev)
-    nb = int(L.mb_decode_attn_workspace_size(T, H, Lk, d))
+    out = torch.empty((T, Hl, d), dtype=torch.float16, device=dev)
+    nb = int(L.mb_decode_attn_workspace_size(T, Hl, Lk, d))
     ws = torch.zeros(nb, dtype=torch.uint8, device=dev)
     st = torch.cuda.Stream(device=dev)
     scale = 1.0 / float(d) ** 0.5
 
     def call(i):
-        k, v = kv[i % 2]
-        rc = L.mb_decode_attn(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), T, H, Lk, d, scale,
+        k, v = kv[i % copies]
+        rc = L.mb_decode_attn(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), T, Hl, Lk, d, scale,
                               tab.data_ptr(), lut.size, 16.0, ws.data_ptr(), nb, st.cuda_stream)
         assert rc == 0, rc
+        if world > 1:
+            gather_heads(out, bounds)
 
     with torch.cuda.stream(st):
         for i in range(4):
             call(i)
         st.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
         for i in range(reps):
@@ -498,14 +513,23 @@ def attention_side(dev, peak, peak_kind, reps: int = 10, with_cpu: bool = True):
         e1.record(st)
         st.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / reps
+    if world > 1:
+        import torch.distributed as dist
+        m = torch.tensor([us], dtype=torch.float64, device=dev)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        us = float(m.item())
     b = attention_bytes(T, H, Lk, d)
     gbs = b / us / 1e3
     del kv, ws
-    return {"workload": "BASELINE config 4: LUT-softmax decode attention, 16 traces x 16 heads, L=4096, d=128",
-            "us_per_call": us, "GBps": gbs, "bytes_per_call": b, "kernels_per_call": 3,
-            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                         "peak_kind": peak_kind},
-            "cpu_baseline": attention_cpu_baseline(T, H, Lk, d) if with_cpu else None}
+    torch.cuda.empty_cache()
+    res = {"workload": "BASELINE config 4: LUT-softmax decode attention, 16 traces x 16 heads, L=4096, d=128"
+                       + (f"; heads sharded over {world} GPUs + NCCL all-gather" if world > 1 else ""),
+           "us_per_call": us, "GBps": gbs, "bytes_per_call": b, "kernels_per_call": 3, "kv_copies": copies,
+           "heads_per_rank": [h1_ - h0_ for h0_, h1_ in bounds],
+           "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
+                        "frac": gbs / world / peak, "peak_kind": peak_kind, "per": "GPU"},
+           "cpu_baseline": attention_cpu_baseline(T, H, Lk, d) if (with_cpu and world == 1) else None}
+    return res
 
 
 def attention_cpu_baseline(T, H, Lk, d, budget_s: float = 6.0):
@@ -531,7 +555,7 @@ def attention_cpu_baseline(T, H, Lk, d, budget_s: float = 6.0):
 
 
 def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 256, prompt: int = 512, check_steps: int = 16,
-                with_cpu: bool = True):
+                with_cpu: bool = True, profile_step: bool = False):
     """BASELINE config 5 as written: a random-init Qwen-1.5B-like INT4 decoder (24
     layers, hidden 2048, 16 heads x 128, FFN 5504, vocab 151936), N = 16 traces, a
     prompt of 512 seeded random token ids run through the decode step one position at
@@ -554,7 +578,7 @@ def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 256, prompt: in
     reported. Reported beside the GEMM line."""
     import torch
     from moat_b200.decode import DecoderConfig, Int4Decoder, timed_decode
-    cfg = DecoderConfig(max_len=prompt + steps + 16)
+    cfg = DecoderConfig(max_len=prompt + steps + 24)
     N = 16
     g = torch.Generator(device=dev)
     g.manual_seed(SEED + 6)
@@ -574,6 +598,11 @@ def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 256, prompt: in
             ms = timed_decode(dec, steps, warmup=3, graph=True)
         except RuntimeError as e:  # raised on every rank alike (the check is all-reduced)
             return {"workload": "BASELINE config 5 decode", "error": str(e), "tensor_parallel": world}
+        if profile_step:  # one eager step inside an NVTX range, for an ncu launch list of one step
+            torch.cuda.nvtx.range_push("decode_step")
+            dec.step(dec.ids)
+            torch.cuda.synchronize()
+            torch.cuda.nvtx.range_pop()
         err = int(dec.err.item())
         wbytes = sum(sum(int(lw[k].numel()) for k in ("wqkv", "wo", "wgu", "wd")) for lw in dec.layers) \
             + int(dec.lm_head.numel())
@@ -671,29 +700,133 @@ def decode_cpu_baseline(dec, snap, ins, outs):
             "ids_compared": int(gpu.size)}
 
 
-def sampling_side(dev, calls: int = 50):
-    """Batched sampler speed on the config-5 LM-head output shape: 16 rows of 151936
-    fp16 logits, temperature 0.7, top-50 of the LUT softmax (``mb_sample_tokens``),
-    CUDA-event timed over back-to-back calls after warm-up."""
+def sampling_side(dev, rows=(16,), calls: int = 50, vocab: int = 151936, temperature: float = 0.7):
+    """Batched sampler speed on the config-5 LM-head output shape: N rows of 151936
+    fp16 logits, temperature 0.7, top-50 of the LUT softmax (``mb_sample_tokens``), as
+    back-to-back eager calls and as one captured CUDA graph of the same calls,
+    CUDA-event timed after warm-up."""
     import torch
     from moat_b200.sampling import BatchSampler
-    N, V = 16, 151936
+    out = {"workload": f"mb_sample_tokens: N x {vocab} fp16 logits, T={temperature}, top-50, LUT range 10",
+           "calls": calls, "rows": {}}
+    for N in rows:
+        g = torch.Generator(device=dev)
+        g.manual_seed(SEED + 9 + N)
+        logits = (torch.randn((N, vocab), generator=g, device=dev) * 3.0).half()
+        s = BatchSampler(N, vocab, device=dev, seed=SEED)
+        for _ in range(5):
+            s.sample(logits, temperature)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(calls):
+            s.sample(logits, temperature)
+        e1.record()
+        torch.cuda.synchronize()
+        eager = e0.elapsed_time(e1) / calls * 1e3
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                for _ in range(calls):
+                    s.sample(logits, temperature)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        out["rows"][str(N)] = {"us_per_call": eager, "graph_us_per_call": e0.elapsed_time(e1) / calls * 1e3,
+                               "device_error_bits": int(s.err.item())}
+        del graph
+    if len(rows) == 1:
+        out["us_per_call"] = out["rows"][str(rows[0])]["us_per_call"]
+    return out
+
+
+def exchange_side(dev, rank: int, world: int, rows: int = 16, hidden: int = 2048, vocab: int = 151936,
+                  iters: int = 200):
+    """The tensor-parallel decode step's exchanges on ``world`` GPUs (``--part
+    exchange`` under torchrun): ``add_rmsnorm`` of [N, D] fp16 partials over NVLink peer
+    stores, the greedy ``argmax`` over [N, V/G] logits per rank, and an NCCL
+    ``all_reduce`` of the same [N, D] fp16 rows for comparison; CUDA events over
+    back-to-back calls after warm-up, the maximum over ranks."""
+    import torch
+    import torch.distributed as dist
+    from moat_b200.peer import PeerExchange
+    N, D = rows, hidden
+    px = PeerExchange(N, D, dev)
     g = torch.Generator(device=dev)
-    g.manual_seed(SEED + 9)
-    logits = (torch.randn((N, V), generator=g, device=dev) * 3.0).half()
-    s = BatchSampler(N, V, device=dev, seed=SEED)
-    for _ in range(5):
-        s.sample(logits, 0.7)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(calls):
-        s.sample(logits, 0.7)
-    e1.record()
-    torch.cuda.synchronize()
-    return {"workload": "mb_sample_tokens: 16 x 151936 fp16 logits, T=0.7, top-50, LUT range 10",
-            "us_per_call": e0.elapsed_time(e1) / calls * 1e3, "calls": calls,
-            "device_error_bits": int(s.err.item())}
+    g.manual_seed(rank)
+    partial = torch.randn((N, D), generator=g, device=dev).half()
+    x = torch.zeros((N, D), device=dev)
+    w = torch.ones(D, device=dev)
+    h = torch.empty((N, D), dtype=torch.float16, device=dev)
+    Vl = vocab // world
+    logits = torch.randn((N, Vl), generator=g, device=dev).half()
+    ids = torch.empty(N, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    red = partial.clone()
+
+    def timed(fn):
+        for _ in range(10):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        m = torch.tensor([e0.elapsed_time(e1) / iters * 1e3], dtype=torch.float64, device=dev)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        return float(m.item())
+
+    try:
+        out = {"world": world, "rows": N, "hidden": D, "vocab_per_rank": Vl, "iters": iters,
+               "add_rmsnorm_us": timed(lambda: px.add_rmsnorm(partial, x, w, 1e-6, h, err)),
+               "argmax_us": timed(lambda: px.argmax(logits, rank * Vl, ids, err)),
+               "nccl_all_reduce_us": timed(lambda: dist.all_reduce(red))}
+        e = err.clone()
+        dist.all_reduce(e, op=dist.ReduceOp.MAX)
+        out["device_error_bits"] = int(e.item())
+    finally:
+        px.close()
+    return out
+
+
+def run_part(args):
+    """``--part decode|sampling|exchange``: one side measurement alone (rank 0 prints
+    its JSON block)."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        if args.part == "decode":
+            out = decode_side(dev, rank, world, steps=args.decode_steps, prompt=args.decode_prompt,
+                              with_cpu=not args.no_cpu, profile_step=args.decode_profile)
+        elif args.part == "sampling":
+            out = sampling_side(dev, rows=tuple(int(r) for r in args.sampling_rows.split(",")))
+        else:
+            if world < 2:
+                raise SystemExit("--part exchange needs torchrun with 2 or more ranks")
+            out = exchange_side(dev, rank, world)
+        if rank == 0:
+            print(json.dumps({"part": args.part, args.part: out}), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    return 0
 
 
 def run_e2e(args, dev, stream, shard, sweep, Ms, world, rank, bounds, R):
@@ -766,11 +899,21 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--e2e-ring", type=int, default=36)
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--part", choices=["all", "decode", "sampling", "exchange"], default="all",
+                    help="run one side measurement alone (decode: BASELINE config 5; sampling: mb_sample_tokens; "
+                         "exchange: the tensor-parallel joins, under torchrun)")
+    ap.add_argument("--decode-steps", type=int, default=256)
+    ap.add_argument("--decode-prompt", type=int, default=512)
+    ap.add_argument("--decode-profile", action="store_true",
+                    help="after timing, one eager decode step inside the NVTX range 'decode_step'")
+    ap.add_argument("--sampling-rows", default="1,16,32")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "moat":
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.part != "all":
+        return run_part(args)
     return run_moat(args)
 
 

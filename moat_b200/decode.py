@@ -449,60 +449,3 @@ def timed_decode(dec: Int4Decoder, steps: int, warmup: int = 3, graph: bool = Tr
 
 
 __all__ = ["DecoderConfig", "Int4Decoder", "rope_table", "timed_decode", "tp_shards"]
-
-
-def main(argv=None) -> int:
-    """``python -m moat_b200.decode``: build the config-5 decoder (random INT4 weights),
-    seed a prompt-length KV cache and time decode steps (CUDA graph replay by default,
-    ``--eager`` for per-kernel launches). Under ``torchrun`` with N processes the
-    decoder is tensor-parallel over N GPUs (the joins inside the graph)."""
-    import argparse
-    import json
-    import os
-    import time
-    from datetime import timedelta
-    ap = argparse.ArgumentParser(description=main.__doc__)
-    ap.add_argument("--traces", type=int, default=16)
-    ap.add_argument("--prompt", type=int, default=512)
-    ap.add_argument("--steps", type=int, default=64)
-    ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--layers", type=int, default=24)
-    ap.add_argument("--eager", action="store_true")
-    ap.add_argument("--temperature", type=float, default=0.0, help="> 0: top-50 sampling")
-    ap.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
-                    help="how tensor-parallel ranks join their partial products (N > 1)")
-    args = ap.parse_args(argv)
-    t = _lib.require_cuda()
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    dev = t.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    t.cuda.set_device(dev)
-    if world > 1:
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    cfg = DecoderConfig(layers=args.layers, max_len=max(768, args.prompt + args.warmup + args.steps + 2))
-    t0 = time.perf_counter()
-    dec = Int4Decoder(cfg, args.traces, device=dev, seed=0, rank=rank, world=world, exchange=args.exchange,
-                      temperature=args.temperature)
-    try:
-        dec.fill_prompt_cache(args.prompt, seed=1)
-        dec.ids.copy_(t.arange(args.traces, dtype=t.int32, device=dec.dev) * 7919 % cfg.vocab)
-        t.cuda.synchronize()
-        build = time.perf_counter() - t0
-        ms = timed_decode(dec, args.steps, args.warmup, graph=not args.eager)
-        if rank == 0:
-            print(json.dumps({"tok_per_s": args.traces / ms * 1e3, "ms_per_step": ms, "traces": args.traces,
-                              "layers": cfg.layers, "prompt": args.prompt, "steps": args.steps, "tp": world,
-                              "exchange": args.exchange if world > 1 else None, "temperature": args.temperature,
-                              "mode": "eager" if args.eager else "graph", "setup_s": build,
-                              "device_error_bits": int(dec.err.item())}))
-    finally:
-        dec.close()  # graph and exchange buffers go before the process group
-        if world > 1:
-            import torch.distributed as dist
-            dist.destroy_process_group()
-    return 0
-
-
-if __name__ == "__main__":
-    raise SystemExit(main())

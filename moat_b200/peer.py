@@ -123,73 +123,3 @@ class PeerExchange:
 
 
 __all__ = ["PeerExchange", "DEVERR_TIMEOUT"]
-
-
-def main(argv=None) -> int:
-    """``torchrun --nproc-per-node G -m moat_b200.peer``: time the exchanges of the
-    tensor-parallel decode step on G GPUs: ``add_rmsnorm`` of [N, D] fp16 partials,
-    ``argmax`` of [N, V/G] logits per rank, and an NCCL ``all_reduce`` of the same
-    [N, D] fp16 for comparison; CUDA events over back-to-back calls after warm-up,
-    the maximum over ranks; rank 0 prints one JSON line."""
-    import argparse
-    import json
-    import os
-    from datetime import timedelta
-
-    import torch.distributed as dist
-    ap = argparse.ArgumentParser(description=main.__doc__)
-    ap.add_argument("--rows", type=int, default=16)
-    ap.add_argument("--hidden", type=int, default=2048)
-    ap.add_argument("--vocab", type=int, default=151936)
-    ap.add_argument("--iters", type=int, default=200)
-    args = ap.parse_args(argv)
-    t = _lib.require_cuda()
-    dev = t.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    t.cuda.set_device(dev)
-    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    world, rank = dist.get_world_size(), dist.get_rank()
-    N, D = args.rows, args.hidden
-    px = PeerExchange(N, D, dev)
-    g = t.Generator(device=dev)
-    g.manual_seed(rank)
-    partial = t.randn((N, D), generator=g, device=dev).half()
-    x = t.zeros((N, D), device=dev)
-    w = t.ones(D, device=dev)
-    h = t.empty((N, D), dtype=t.float16, device=dev)
-    Vl = args.vocab // world
-    logits = t.randn((N, Vl), generator=g, device=dev).half()
-    ids = t.empty(N, dtype=t.int32, device=dev)
-    err = t.zeros(1, dtype=t.int32, device=dev)
-    red = partial.clone()
-
-    def timed(fn):
-        for _ in range(10):
-            fn()
-        t.cuda.synchronize()
-        dist.barrier()
-        e0, e1 = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.iters):
-            fn()
-        e1.record()
-        t.cuda.synchronize()
-        m = t.tensor([e0.elapsed_time(e1) / args.iters * 1e3], dtype=t.float64, device=dev)
-        dist.all_reduce(m, op=dist.ReduceOp.MAX)
-        return float(m.item())
-
-    out = {"world": world, "rows": N, "hidden": D, "vocab_per_rank": Vl, "iters": args.iters,
-           "add_rmsnorm_us": timed(lambda: px.add_rmsnorm(partial, x, w, 1e-6, h, err)),
-           "argmax_us": timed(lambda: px.argmax(logits, rank * Vl, ids, err)),
-           "nccl_all_reduce_us": timed(lambda: dist.all_reduce(red))}
-    e = err.clone()
-    dist.all_reduce(e, op=dist.ReduceOp.MAX)
-    out["device_error_bits"] = int(e.item())
-    px.close()
-    if rank == 0:
-        print(json.dumps(out))
-    dist.destroy_process_group()
-    return 0
-
-
-if __name__ == "__main__":
-    raise SystemExit(main())

@@ -104,59 +104,3 @@ def sample_tokens(logits_batch, temperature: float = 0.7, top_p: float = 0.9, *,
 
 
 __all__ = ["BatchSampler", "sample_tokens", "TOP_K"]
-
-
-def main(argv=None) -> int:
-    """``python -m moat_b200.sampling``: time ``mb_sample_tokens`` on seeded fp16 logits
-    [N, V] (default: the config-5 LM-head shape, V = 151936) for each N given, as 50
-    back-to-back eager calls and as one captured CUDA graph of the same 50 calls,
-    CUDA-event timed after warm-up; prints one JSON line."""
-    import argparse
-    import json
-    ap = argparse.ArgumentParser(description=main.__doc__)
-    ap.add_argument("--rows", type=int, nargs="+", default=[1, 16, 32])
-    ap.add_argument("--vocab", type=int, default=151936)
-    ap.add_argument("--temperature", type=float, default=0.7)
-    ap.add_argument("--calls", type=int, default=50)
-    args = ap.parse_args(argv)
-    t = _lib.require_cuda()
-    dev = t.device("cuda", t.cuda.current_device())
-    out = {"vocab": args.vocab, "temperature": args.temperature, "calls": args.calls, "rows": {}}
-    for N in args.rows:
-        g = t.Generator(device=dev)
-        g.manual_seed(N)
-        logits = (t.randn((N, args.vocab), generator=g, device=dev) * 3.0).half()
-        s = BatchSampler(N, args.vocab, device=dev, seed=1)
-        for _ in range(5):
-            s.sample(logits, args.temperature)
-        t.cuda.synchronize()
-        e0, e1 = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.calls):
-            s.sample(logits, args.temperature)
-        e1.record()
-        t.cuda.synchronize()
-        eager = e0.elapsed_time(e1) / args.calls * 1e3
-        graph = t.cuda.CUDAGraph()
-        side = t.cuda.Stream(device=dev)
-        side.wait_stream(t.cuda.current_stream(dev))
-        with t.cuda.stream(side):
-            with t.cuda.graph(graph, stream=side):
-                for _ in range(args.calls):
-                    s.sample(logits, args.temperature)
-        t.cuda.current_stream(dev).wait_stream(side)
-        graph.replay()
-        t.cuda.synchronize()
-        e0.record()
-        graph.replay()
-        e1.record()
-        t.cuda.synchronize()
-        out["rows"][N] = {"eager_us": eager, "graph_us": e0.elapsed_time(e1) / args.calls * 1e3,
-                          "device_error_bits": int(s.err.item())}
-        del graph
-    print(json.dumps(out))
-    return 0
-
-
-if __name__ == "__main__":
-    raise SystemExit(main())
