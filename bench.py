@@ -752,7 +752,9 @@ def exchange_side(dev, rank: int, world: int, rows: int = 16, hidden: int = 2048
     exchange`` under torchrun): ``add_rmsnorm`` of [N, D] fp16 partials over NVLink peer
     stores, the greedy ``argmax`` over [N, V/G] logits per rank, and an NCCL
     ``all_reduce`` of the same [N, D] fp16 rows for comparison; CUDA events over
-    back-to-back calls after warm-up, the maximum over ranks."""
+    back-to-back calls after warm-up, the maximum over ranks. ``*_us``: the calls
+    replayed from one CUDA graph, as in the decode step; ``*_eager_us``: launched one by
+    one from Python (host-bound)."""
     import torch
     import torch.distributed as dist
     from moat_b200.peer import PeerExchange
@@ -770,26 +772,44 @@ def exchange_side(dev, rank: int, world: int, rows: int = 16, hidden: int = 2048
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     red = partial.clone()
 
-    def timed(fn):
+    def timed(fn, graph):
+        """Microseconds per call, max over ranks: ``iters`` calls replayed from one CUDA
+        graph (as the decode step runs them) or launched eagerly from the host."""
         for _ in range(10):
             fn()
         torch.cuda.synchronize()
+        g = None
+        if graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(iters):
+                    fn()
+            g.replay()
+            torch.cuda.synchronize()
         dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(iters):
-            fn()
+        if graph:
+            g.replay()
+        else:
+            for _ in range(iters):
+                fn()
         e1.record()
         torch.cuda.synchronize()
+        del g  # a graph holding NCCL calls is released before the process group
         m = torch.tensor([e0.elapsed_time(e1) / iters * 1e3], dtype=torch.float64, device=dev)
         dist.all_reduce(m, op=dist.ReduceOp.MAX)
         return float(m.item())
 
+    calls = {"add_rmsnorm": lambda: px.add_rmsnorm(partial, x, w, 1e-6, h, err),
+             "argmax": lambda: px.argmax(logits, rank * Vl, ids, err),
+             "nccl_all_reduce": lambda: dist.all_reduce(red)}
     try:
-        out = {"world": world, "rows": N, "hidden": D, "vocab_per_rank": Vl, "iters": iters,
-               "add_rmsnorm_us": timed(lambda: px.add_rmsnorm(partial, x, w, 1e-6, h, err)),
-               "argmax_us": timed(lambda: px.argmax(logits, rank * Vl, ids, err)),
-               "nccl_all_reduce_us": timed(lambda: dist.all_reduce(red))}
+        out = {"world": world, "rows": N, "hidden": D, "vocab_per_rank": Vl, "iters": iters}
+        for name, fn in calls.items():
+            out[f"{name}_us"] = timed(fn, graph=True)
+        for name, fn in calls.items():
+            out[f"{name}_eager_us"] = timed(fn, graph=False)
         e = err.clone()
         dist.all_reduce(e, op=dist.ReduceOp.MAX)
         out["device_error_bits"] = int(e.item())

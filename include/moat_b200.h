@@ -254,9 +254,13 @@ int32_t mb_argmax_keys_to_ids(const int64_t* keys, int32_t N, int32_t* ids, void
  * The reference runs on one device; these entry points join the Megatron shards of
  * its decode step (transformer.py:148-158 residual + RMSNorm after o_proj and down;
  * batch_generator.py:203-206 greedy choice after lm_head) without a library
- * collective: each rank stores its rows into the other ranks' exchange buffers
- * (CUDA IPC mappings, plain peer stores, no multicast), raises a release flag and
- * waits, bounded by timeout_ns, for every rank's rows. A wait that expires sets
+ * collective: each rank stores its rows into every rank's exchange buffer (CUDA IPC
+ * mappings, plain peer stores, no multicast) as 8-byte words that each carry 4 bytes
+ * of payload and the call's epoch, so a word whose epoch matches is itself the proof
+ * that its payload arrived (no fence, no separate flag), and polls its own buffer,
+ * bounded by timeout_ns, until every word it reads carries the epoch. Two slot sets
+ * alternate by epoch parity, so a fast rank's next call never overwrites words a slow
+ * rank has still to read. A wait that expires sets
  * MB_DEVERR_TIMEOUT in dev_err; the outputs of that call are then undefined.
  * bufs[q] is rank q's exchange buffer as mapped in this process (bufs[rank] its own),
  * each of mb_peer_buffer_bytes(max_rows, D) bytes, zeroed before the first call.

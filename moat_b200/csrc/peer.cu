@@ -16,12 +16,15 @@
 // Every rank sums the same values in the same order, so the residual streams stay
 // bit-identical across ranks.
 //
-// Exchange buffer (one per rank, cudaMalloc + CUDA IPC, zeroed at creation):
-//   [0, 2048)            flags of channel 0 (add_rmsnorm): uint32 [kMaxRows][kMaxRanks]
-//   [2048, 4096)         flags of channel 1 (argmax)
-//   [4096, 12288)        channel 1 keys: int64 [2 parities][kMaxRanks][kMaxRows]
-//   [16384, ...)         channel 0 rows: fp16 [2 parities][kMaxRanks][slot_elems]
-// flags[n][q] at rank r holds the last epoch in which rank q delivered row n to r.
+// Exchange buffer (one per rank, cudaMalloc + CUDA IPC, zeroed at creation), written
+// by the other ranks with 8-byte "low-latency" words: 4 bytes of payload and 4 bytes
+// holding the epoch of the call that wrote them, stored in one transaction, so a
+// receiver that reads a word carrying the current epoch has its payload too (no fence,
+// no separate flag, one NVLink crossing per word):
+//   [0, 16384)      channel 1 (argmax): [2 parities][kMaxRanks][kMaxRows] keys, each
+//                   two words (low and high 32 bits of the 64-bit key)
+//   [16384, ...)    channel 0 (add_rmsnorm) rows: [2 parities][kMaxRanks][slot_elems / 2]
+//                   words, two fp16 per word
 // Epoch e (1, 2, ...) of a channel writes parity e & 1; a rank can only reach epoch
 // e + 2 after every rank has finished epoch e + 1, hence finished reading epoch e's
 // parity, so two parities never race. The epoch counter of each channel lives in a
@@ -49,10 +52,9 @@ namespace mb {
 constexpr int kPeerMaxRanks = 8;
 constexpr int kPeerMaxRows = 64;
 constexpr int kPeerBlock = 256;
-constexpr size_t kPeerFlagBytes = sizeof(uint32_t) * kPeerMaxRows * kPeerMaxRanks;  // 2048 per channel
-constexpr size_t kPeerKeyOff = 2 * kPeerFlagBytes;
+constexpr size_t kPeerKeyOff = 0;
 constexpr size_t kPeerRowOff = 16384;
-static_assert(kPeerKeyOff + 2 * kPeerMaxRanks * kPeerMaxRows * sizeof(int64_t) <= kPeerRowOff, "layout");
+static_assert(kPeerKeyOff + 2 * kPeerMaxRanks * kPeerMaxRows * 2 * sizeof(uint2) <= kPeerRowOff, "layout");
 
 struct PeerSet {
   uint8_t* buf[kPeerMaxRanks];  // every rank's exchange buffer as mapped in this process (own included)
@@ -62,46 +64,39 @@ struct PeerSet {
   int64_t timeout_ns;
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
 
-__device__ __forceinline__ uint32_t* peer_flag(uint8_t* buf, int channel, int row, int src) {
-  return reinterpret_cast<uint32_t*>(buf + channel * kPeerFlagBytes) + row * kPeerMaxRanks + src;
+// One low-latency word: payload and epoch in a single 8-byte store / load.
+__device__ __forceinline__ void st_ll(uint2* p, uint32_t payload, uint32_t epoch) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(payload), "r"(epoch) : "memory");
 }
 
-// Publish this CTA's stores (all threads, before the barrier) to every rank, then wait
-// for every rank's row `row` of epoch `epoch`. Threads q < world each own one rank.
-__device__ __forceinline__ void peer_signal_and_wait(const PeerSet& ps, int channel, int row, uint32_t epoch,
-                                                     uint32_t* err) {
-  __syncthreads();
-  const int q = threadIdx.x;
-  if (q < ps.world) {
-    __threadfence_system();
-    st_release_sys(peer_flag(ps.buf[q], channel, row, ps.rank), epoch);
-    const uint32_t* f = peer_flag(ps.buf[ps.rank], channel, row, q);
-    const uint64_t t0 = global_ns();
-    while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
-      if (global_ns() - t0 > static_cast<uint64_t>(ps.timeout_ns)) {
-        if (err) atomicOr(err, MB_DEVERR_TIMEOUT);
-        break;
-      }
-      __nanosleep(64);
+__device__ __forceinline__ uint2 ld_ll(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+
+// The payload of word `p` once it carries `epoch`; waits at most until `deadline`
+// (global ns), then sets MB_DEVERR_TIMEOUT and returns whatever the word holds.
+__device__ __forceinline__ uint32_t wait_ll(const uint2* p, uint32_t epoch, uint64_t& deadline, int64_t timeout_ns,
+                                            uint32_t* err) {
+  uint2 v = ld_ll(p);
+  if (v.y == epoch) return v.x;
+  if (deadline == 0) deadline = global_ns() + static_cast<uint64_t>(timeout_ns);
+  while (v.y != epoch) {
+    if (global_ns() > deadline) {
+      if (err) atomicOr(err, MB_DEVERR_TIMEOUT);
+      deadline = 1;  // expired: later words of this call do not wait again
+      break;
     }
+    v = ld_ll(p);
   }
-  __syncthreads();
+  return v.x;
 }
 
 // The last CTA of a call advances the channel's epoch (read by the next call).
@@ -140,29 +135,36 @@ __global__ void __launch_bounds__(kPeerBlock) k_peer_add_rmsnorm(PeerSet ps, con
   const int n = blockIdx.x;
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(state) + 1u;
   const int par = epoch & 1u;
-  const int vecs = D / 8;  // 16-byte vectors per row
+  const int chunks = D / 8;  // 16-byte chunks of a row: four words each
   auto slot = [&](uint8_t* buf, int src) {
-    return reinterpret_cast<uint4*>(buf + kPeerRowOff) +
-           ((static_cast<int64_t>(par) * kPeerMaxRanks + src) * ps.slot_elems + static_cast<int64_t>(n) * D) / 8;
+    return reinterpret_cast<uint2*>(buf + kPeerRowOff) +
+           ((static_cast<int64_t>(par) * kPeerMaxRanks + src) * ps.slot_elems + static_cast<int64_t>(n) * D) / 2;
   };
-  // 1. this rank's row n into slot [par][rank] of every rank (its own buffer included)
+  // 1. this rank's row n as low-latency words into slot [par][rank] of every rank
   const uint4* src = reinterpret_cast<const uint4*>(partial + static_cast<int64_t>(n) * D);
-  for (int i = threadIdx.x; i < vecs; i += kPeerBlock) {
+  for (int i = threadIdx.x; i < chunks; i += kPeerBlock) {
     const uint4 v = src[i];
-    for (int q = 0; q < ps.world; ++q) slot(ps.buf[q], ps.rank)[i] = v;
+    for (int q = 0; q < ps.world; ++q) {
+      uint2* d = slot(ps.buf[q], ps.rank) + 4 * i;
+      st_ll(d, v.x, epoch);
+      st_ll(d + 1, v.y, epoch);
+      st_ll(d + 2, v.z, epoch);
+      st_ll(d + 3, v.w, epoch);
+    }
   }
-  peer_signal_and_wait(ps, 0, n, epoch, err);
-  // 2. sum the ranks' rows in rank order (fp32), one fp16 rounding
-  for (int i = threadIdx.x; i < vecs; i += kPeerBlock) {
+  // 2. every rank's words of the same chunks (own buffer), summed in rank order in fp32,
+  //    one fp16 rounding
+  uint64_t deadline = 0;
+  for (int i = threadIdx.x; i < chunks; i += kPeerBlock) {
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
     for (int q = 0; q < ps.world; ++q) {
-      const uint4 v = __ldcg(slot(ps.buf[ps.rank], q) + i);
-      const __half2* hv = reinterpret_cast<const __half2*>(&v);
+      const uint2* s0 = slot(ps.buf[ps.rank], q) + 4 * i;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float2 f = __half22float2(hv[j]);
+        const uint32_t word = wait_ll(s0 + j, epoch, deadline, ps.timeout_ns, err);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&word));
         acc[2 * j] += f.x;
         acc[2 * j + 1] += f.y;
       }
@@ -208,20 +210,26 @@ __global__ void __launch_bounds__(kPeerArgBlock) k_peer_argmax(PeerSet ps, const
   if ((threadIdx.x & 31) == 0) best_w[threadIdx.x >> 5] = best;
   __syncthreads();
   auto key_slot = [&](uint8_t* buf, int src) {
-    return reinterpret_cast<unsigned long long*>(buf + kPeerKeyOff) + (par * kPeerMaxRanks + src) * kPeerMaxRows + n;
+    return reinterpret_cast<uint2*>(buf + kPeerKeyOff) + 2 * ((par * kPeerMaxRanks + src) * kPeerMaxRows + n);
   };
+  __shared__ unsigned long long got[kPeerMaxRanks];
   if (threadIdx.x < ps.world) {
     unsigned long long b = best_w[0];
     for (int i = 1; i < kPeerArgBlock / 32; ++i) b = best_w[i] > b ? best_w[i] : b;
-    *key_slot(ps.buf[threadIdx.x], ps.rank) = b;
+    uint2* d = key_slot(ps.buf[threadIdx.x], ps.rank);
+    st_ll(d, static_cast<uint32_t>(b), epoch);
+    st_ll(d + 1, static_cast<uint32_t>(b >> 32), epoch);
+    // rank threadIdx.x's key for this row, from this rank's buffer
+    uint64_t deadline = 0;
+    const uint2* s0 = key_slot(ps.buf[ps.rank], threadIdx.x);
+    const uint32_t lo = wait_ll(s0, epoch, deadline, ps.timeout_ns, err);
+    const uint32_t hi = wait_ll(s0 + 1, epoch, deadline, ps.timeout_ns, err);
+    got[threadIdx.x] = (static_cast<unsigned long long>(hi) << 32) | lo;
   }
-  peer_signal_and_wait(ps, 1, n, epoch, err);
+  __syncthreads();
   if (threadIdx.x == 0) {
     unsigned long long b = 0;
-    for (int q = 0; q < ps.world; ++q) {
-      const unsigned long long k = __ldcg(key_slot(ps.buf[ps.rank], q));
-      b = k > b ? k : b;
-    }
+    for (int q = 0; q < ps.world; ++q) b = got[q] > b ? got[q] : b;
     ids[n] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(b & 0xFFFFFFFFull));
   }
   peer_finish(state, epoch);
@@ -251,8 +259,8 @@ extern "C" {
 
 size_t mb_peer_buffer_bytes(int32_t max_rows, int32_t D) {
   if (max_rows < 1 || max_rows > kPeerMaxRows || D < 8 || D % 8 != 0) return 0;
-  const size_t slot = static_cast<size_t>(max_rows) * D;
-  return kPeerRowOff + 2 * kPeerMaxRanks * slot * sizeof(uint16_t);
+  const size_t slot = static_cast<size_t>(max_rows) * D;  // fp16 elements; two per 8-byte word
+  return kPeerRowOff + 2 * kPeerMaxRanks * (slot / 2) * sizeof(uint2);
 }
 
 int32_t mb_ipc_alloc(size_t bytes, void** ptr, uint8_t* handle) {

@@ -118,7 +118,9 @@ def test_host_side_argument_validation(L):
 def test_tensor_parallel_and_sampling_entries_validate_on_the_host(L):
     fake = ctypes.c_void_p(0x10000)
     bufs = (ctypes.c_void_p * 2)(0x10000, 0x20000)
-    assert L.mb_peer_buffer_bytes(16, 2048) == 16384 + 2 * 8 * 16 * 2048 * 2
+    # key words, then two parities x 8 ranks of row slots; every 8-byte word carries
+    # two bf16 payload values and the call's epoch
+    assert L.mb_peer_buffer_bytes(16, 2048) == 16384 + 2 * 8 * (16 * 2048 // 2) * 8
     assert L.mb_peer_buffer_bytes(0, 2048) == 0 and L.mb_peer_buffer_bytes(65, 2048) == 0
     assert L.mb_peer_buffer_bytes(16, 100) == 0
     assert L.mb_argmax_key_f16(None, 2, 10, 0, fake, None) == -1
