@@ -16,6 +16,9 @@
 //      chunk into a per-chunk slot; the last chunk to arrive sums the slots in chunk
 //      order (deterministic) and writes the fp16 output. The workspace needs no
 //      initial contents (pass 1 resets the arrival counters).
+// Rows of up to 2048 keys (the decode step's caches) take one launch instead: one CTA
+// per row streams its K and then its V rows through a shared-memory ring with bulk
+// copies, holding the row's scores in shared memory (k_attn_stream).
 #include <algorithm>
 
 #include "common.cuh"
@@ -451,6 +454,214 @@ __global__ void __launch_bounds__(kAttnBlock) k_attn_fused(const uint16_t* __res
   }
 }
 
+// ---------------------------------------------------------------------------
+// Streaming path for rows of up to kAttnStreamMax keys (the decode step's caches):
+// one CTA per (trace, head) row, no workspace, one launch. A producer warp streams the
+// row's K rows and then its V rows through a ring of kStrRing shared-memory stages with
+// bulk copies (cp.async.bulk, no multicast, completion on mbarriers), so the V stream
+// starts while the last scores are formed and the memory system always holds a full
+// ring of this row's requests. Eight consumer warps:
+//   1. scores of every K stage -> shared memory (16-byte slices of a key per lane,
+//      xor-shuffle sum over the d / 8 lanes of a key), row max;
+//   2. e_l = LUT(s_l - max) in place and their sum (the strided-then-block order of
+//      k_attn_stats), then p_l = fp16(e_l / sum) in place;
+//   3. P.V over every V stage as it lands, fp32; per-warp partials summed in warp order.
+// Per element the arithmetic is that of the split passes; the order of the output sum
+// differs. Deterministic.
+// ---------------------------------------------------------------------------
+constexpr int kAttnStreamMax = 2048;  // keys per row held as scores in shared memory
+constexpr int kStrWarps = 8;          // consumer warps
+constexpr int kStrStage = 32768;      // bytes per ring stage
+constexpr int kStrRing = 3;           // ring stages
+
+__device__ __forceinline__ void bulk_load_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4u(const void* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(smem_u32(p)));
+  return v;
+}
+
+// Block reductions over the consumer warps only (named barrier 1; the producer warp
+// takes no part).
+__device__ __forceinline__ float cons_reduce(float v, float* sh, bool is_max) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? nanmax_f(v, u) : v + u;
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  named_bar_sync(1, kStrWarps * 32);
+  if (l == 0) sh[w] = v;
+  named_bar_sync(1, kStrWarps * 32);
+  v = sh[0];
+  for (int i = 1; i < kStrWarps; ++i) v = is_max ? nanmax_f(v, sh[i]) : v + sh[i];
+  return v;
+}
+
+template <int TPR>
+__global__ void __launch_bounds__((kStrWarps + 1) * 32) k_attn_stream(const uint16_t* __restrict__ q,
+                                                                      const uint16_t* __restrict__ k,
+                                                                      const uint16_t* __restrict__ v,
+                                                                      uint16_t* __restrict__ out, int Lg, int64_t kvs,
+                                                                      float scale, const uint16_t* __restrict__ table,
+                                                                      int size, float step, AttnWs w) {
+  constexpr int D = TPR * 8;
+  constexpr int KS = kStrStage / (D * 2);  // keys per stage
+  constexpr int KW = 32 / TPR;             // keys per warp step
+  constexpr int IT = KS / (kStrWarps * KW);  // warp steps per stage (8 for every d)
+  constexpr int CT = kStrWarps * 32;
+  static_assert(IT * kStrWarps * KW == KS, "stage split");
+  extern __shared__ __align__(128) uint8_t dyn[];
+  uint8_t* ring = dyn;                                                   // [kStrRing][kStrStage]
+  float* sc = reinterpret_cast<float*>(dyn + kStrRing * kStrStage);      // [Lg]
+  float* red = sc + ((Lg + 3) & ~3);                                     // [kStrWarps][D]
+  __shared__ __align__(8) uint64_t full[kStrRing], empty[kStrRing];
+  __shared__ float sh[kStrWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x;
+  if (threadIdx.x == 0) {
+    for (int r = 0; r < kStrRing; ++r) {
+      mbar_init(full + r, 1);
+      mbar_init(empty + r, kStrWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_wait();  // q, K, V and the lengths may come from the previous kernel
+  pdl_launch_dependents();
+  const int L = attn_len(w, row, Lg);
+  const int nK = (L + KS - 1) / KS;  // K stages, then as many V stages
+  if (warp == kStrWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();  // every cache byte is read once per call
+      const uint8_t* kb = reinterpret_cast<const uint8_t*>(k + static_cast<int64_t>(row) * kvs);
+      const uint8_t* vb = reinterpret_cast<const uint8_t*>(v + static_cast<int64_t>(row) * kvs);
+      for (int s = 0; s < 2 * nK; ++s) {
+        const int slot = s % kStrRing;
+        if (s >= kStrRing && !mbar_wait(empty + slot, ((s / kStrRing) - 1) & 1) && w.err)
+          atomicOr(w.err, MB_DEVERR_TIMEOUT);
+        const int kk = s < nK ? s : s - nK;
+        const uint32_t bytes = static_cast<uint32_t>(min(KS, L - kk * KS)) * D * 2;
+        mbar_expect_tx(full + slot, bytes);
+        bulk_load_g2s(ring + slot * kStrStage, (s < nK ? kb : vb) + static_cast<size_t>(kk) * KS * D * 2, bytes,
+                      full + slot, pol);
+      }
+    }
+    return;
+  }
+  // ---------------- consumers ----------------
+  const int sub = lane % TPR, ks = lane / TPR;  // 16-byte slice of d, key slot of the warp step
+  float qf[8];
+  {
+    const uint4 qv = *reinterpret_cast<const uint4*>(q + static_cast<int64_t>(row) * D + sub * 8);
+    const __half2* h = reinterpret_cast<const __half2*>(&qv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      qf[2 * i] = f.x;
+      qf[2 * i + 1] = f.y;
+    }
+  }
+  float m = -INFINITY;
+  for (int s = 0; s < nK; ++s) {
+    const int slot = s % kStrRing;
+    if (!mbar_wait(full + slot, (s / kStrRing) & 1) && lane == 0 && w.err) atomicOr(w.err, MB_DEVERR_TIMEOUT);
+    const int j0 = s * KS, rows = min(KS, L - j0);
+    const uint8_t* st = ring + slot * kStrStage;
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      const int kr = (it * kStrWarps + warp) * KW + ks;
+      float dot = 0.0f;
+      if (kr < rows) {
+        const uint4 kv = ld_shared_v4u(st + kr * D * 2 + sub * 16);
+        const __half2* h = reinterpret_cast<const __half2*>(&kv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h[i]);
+          dot = fmaf(qf[2 * i], f.x, dot);
+          dot = fmaf(qf[2 * i + 1], f.y, dot);
+        }
+      }
+#pragma unroll
+      for (int o = TPR / 2; o >= 1; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      if (sub == 0 && kr < rows) {
+        const float x = dot * scale;
+        sc[j0 + kr] = x;
+        m = nanmax_f(m, x);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + slot);
+  }
+  m = cons_reduce(m, sh, true);  // every score is in sc[]
+  float acc = 0.0f;
+  for (int j = threadIdx.x; j < L; j += CT) {
+    const float e = lut_exp(table, sc[j] - m, step, size);
+    sc[j] = e;
+    acc += e;
+  }
+  acc = cons_reduce(acc, sh, false);
+  const float sum = acc > 0.0f ? acc : 1.0f;
+  for (int j = threadIdx.x; j < L; j += CT) sc[j] = __half2float(__float2half_rn(__fdiv_rn(sc[j], sum)));
+  named_bar_sync(1, CT);  // every p_l is in sc[]
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+  for (int s = nK; s < 2 * nK; ++s) {
+    const int slot = s % kStrRing;
+    if (!mbar_wait(full + slot, (s / kStrRing) & 1) && lane == 0 && w.err) atomicOr(w.err, MB_DEVERR_TIMEOUT);
+    const int j0 = (s - nK) * KS, rows = min(KS, L - j0);
+    const uint8_t* st = ring + slot * kStrStage;
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      const int kr = (it * kStrWarps + warp) * KW + ks;
+      if (kr < rows) {
+        const float p = sc[j0 + kr];
+        const uint4 vv = ld_shared_v4u(st + kr * D * 2 + sub * 16);
+        const __half2* h = reinterpret_cast<const __half2*>(&vv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h[i]);
+          o[2 * i] = fmaf(p, f.x, o[2 * i]);
+          o[2 * i + 1] = fmaf(p, f.y, o[2 * i + 1]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + slot);
+  }
+  // the KW key slots of a warp hold the same slice of d: sum them, then the warps
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int x = TPR; x < 32; x <<= 1) o[i] += __shfl_xor_sync(0xffffffffu, o[i], x);
+  if (ks == 0)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[warp * D + sub * 8 + i] = o[i];
+  named_bar_sync(1, CT);
+  for (int dd = threadIdx.x; dd < D; dd += CT) {
+    float t = 0.0f;
+    for (int g = 0; g < kStrWarps; ++g) t += red[g * D + dd];
+    out[static_cast<int64_t>(row) * D + dd] = __half_as_ushort(__float2half_rn(t));
+  }
+}
+
+static size_t attn_stream_smem(int Lg, int d) {
+  return static_cast<size_t>(kStrRing) * kStrStage + static_cast<size_t>((Lg + 3) & ~3) * 4 +
+         static_cast<size_t>(kStrWarps) * d * 4;
+}
+
 static inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 static AttnWs carve_attn_ws(void* base, int T, int H, int L, int d, int C, size_t* total) {
@@ -512,7 +723,17 @@ template <int TPR>
 static int32_t attn_launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int L, int64_t kvs,
                            int C, int rows, float scale, const uint16_t* table, int size, float step, const AttnWs& w,
                            cudaStream_t st) {
-  if (L <= kAttnFusedMax) {  // one CTA per row, scores in shared memory
+  if (L <= kAttnFusedMax) {
+    const bool aligned = ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) == 0;
+    if (aligned && L <= kAttnStreamMax) {  // kvs * 2 bytes is a multiple of 16 for every d >= 8
+      const size_t smem = attn_stream_smem(L, TPR * 8);
+      if (cudaFuncSetAttribute(k_attn_stream<TPR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem)) != cudaSuccess)
+        return MB_ERR_LAUNCH;
+      return launch_with_pdl(k_attn_stream<TPR>, dim3(rows), dim3((kStrWarps + 1) * 32), smem, st, q, k, v, out, L,
+                             kvs, scale, table, size, step, w);
+    }
+    // one CTA per row, scores in shared memory
     const int smem = L * 4;
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(k_attn_fused<TPR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
