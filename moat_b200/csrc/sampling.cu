@@ -17,22 +17,29 @@
 // makes the reference raise; here it sets MB_DEVERR_NONFINITE, token = the argmax,
 // logprob = NaN.
 //
-// One cluster of C <= 8 CTAs (1024 threads each) per row, CTA r owning a contiguous
-// column range; row-wide sums, maxima and histograms are joined through distributed
-// shared memory:
-//   A  max and first argmax of the raw logits (the scaled maximum is the scaled value
-//      at that column: the scaling is monotone);
-//   B  per element the table index of (s - max) into a uint16 scratch row, and the
-//      exact sum of the table values (uint64);
-//   p16 table: for every table index its fp16 probability fp16(e / sum), in shared
-//      memory (the probability of an element is a function of its index alone);
-//   C, D  256-bin histograms of the high, then the low byte of the fp16 probability
-//      bits give the k-th largest probability t;
-//   E  every column with p > t, and the first (k - #{p > t}) columns with p == t in
-//      column order (per-thread contiguous ranges, a block prefix sum, and the tie
-//      counts of the lower-ranked CTAs);
-//   the leader CTA gathers the <= 64 candidate keys (p << 32 | ~column), a warp ranks
-//   them, thread 0 draws.
+// One cluster of C <= 16 CTAs (1024 threads each) per row, CTA r owning a contiguous
+// column range of a multiple of 8 columns (8-column groups, one 16-byte load each when
+// the rows are aligned), and a 16-bit column buffer of table indices per CTA in shared
+// memory (in the global scratch row when it does not fit). Three row-wide joins, each
+// a push of partials into the other CTAs' shared memory (distributed shared memory)
+// and one cluster barrier:
+//   A  max and first argmax of the raw logits, on order-preserving integer codes (the
+//      scaled maximum is the scaled value at that column: the scaling is monotone);
+//   B  per column the table index j of (s - max): the index is a non-increasing
+//      function of the column's code, so a per-CTA table of the highest codes below the
+//      maximum gives it by one lookup, and every code below a table whose lowest entry
+//      clips (most of a row) gets the clip index size - 1 by one compare; j goes to the
+//      column buffer, the exact sum of the table values is joined (uint64 units of
+//      2^-24);
+//   C..E  the probability p(j) = fp16(table[S-1-j] / sum) is a non-increasing function
+//      of j, and the row's top-k by (p descending, column ascending) lies in the union
+//      of the CTAs' own top-k: each CTA finds its k-th smallest index j_k (a high-bit
+//      histogram, then one of the low 7 bits inside the chosen bin), the indices
+//      [j_lo, j_hi] whose probability equals p(j_k) (two warps, 32-way searches of p),
+//      and takes every column below j_lo and the first ties in column order (a block
+//      prefix sum); it sorts these keys (p << 32 | ~column) and pushes them to the
+//      leader CTA, which ranks every key of the union by binary searches in the
+//      other lists, and thread 0 draws.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -44,6 +51,9 @@ namespace mb {
 
 constexpr int kSampBlock = 1024;
 constexpr int kSampMaxK = 64;
+constexpr int kSampMaxCluster = 16;  // CTAs per row (sizes above 8 are non-portable)
+constexpr int kSampLd = 1;           // 8-column groups whose loads a thread issues together
+constexpr int kSampLutMax = 4096;    // codes below the maximum in the code -> index table
 
 __device__ __forceinline__ int samp_lut_index(float x, float step, int size) {
   float f = __fdiv_rn(fabsf(x), step);
@@ -61,12 +71,17 @@ struct SampArgs {
   const uint16_t* table;
   int size;
   float step;
+  float clip;  // |s - max| >= clip implies table index size - 1 (no division needed)
   const float* uniforms;  // [N] or null
   unsigned long long seed;
   uint32_t* rng_state;  // {counter, arrivals}
   int32_t* tokens;
   float* logprobs;
-  uint16_t* scratch;  // [N][V] table indices
+  uint16_t* scratch;  // [N][V] column buffers when a CTA's columns do not fit shared memory
+  int chunk;          // columns per CTA of a cluster (a multiple of 8)
+  int buf_smem;       // 1: the column buffer lives in shared memory after the table
+  int lut_off;        // code -> index table: offset (uint16 entries) in dynamic shared memory
+  int lut_cap;        // and capacity (entries)
   uint32_t* err;
 };
 
@@ -88,20 +103,25 @@ __device__ __forceinline__ unsigned long long splitmix64(unsigned long long z) {
   return z ^ (z >> 31);
 }
 
-// Block reductions (1024 threads = 32 warps); `red` holds 32 slots.
-__device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v, unsigned long long* red) {
+// Block reductions (1024 threads = 32 warps) whose result only warp 0 needs (it pushes
+// the CTA's partial to the cluster): the warps' partials meet in `red` (32 slots), and
+// warp 0 reduces them with shuffles. Both barriers also order every earlier
+// shared-memory write of the block before whatever warp 0 does next.
+__device__ __forceinline__ unsigned long long block_sum_u64_w0(unsigned long long v, unsigned long long* red) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   __syncthreads();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-  unsigned long long t = 0;
+  if (threadIdx.x < 32) {
+    v = red[threadIdx.x];
 #pragma unroll
-  for (int w = 0; w < kSampBlock / 32; ++w) t += red[w];
-  return t;
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  }
+  return v;
 }
 
-__device__ __forceinline__ unsigned long long block_max_u64(unsigned long long v, unsigned long long* red) {
+__device__ __forceinline__ unsigned long long block_max_u64_w0(unsigned long long v, unsigned long long* red) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     const unsigned long long x = __shfl_xor_sync(0xffffffffu, v, o);
@@ -110,10 +130,15 @@ __device__ __forceinline__ unsigned long long block_max_u64(unsigned long long v
   __syncthreads();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-  unsigned long long t = 0;
+  if (threadIdx.x < 32) {
+    v = red[threadIdx.x];
 #pragma unroll
-  for (int w = 0; w < kSampBlock / 32; ++w) t = red[w] > t ? red[w] : t;
-  return t;
+    for (int o = 16; o; o >>= 1) {
+      const unsigned long long x = __shfl_xor_sync(0xffffffffu, v, o);
+      v = x > v ? x : v;
+    }
+  }
+  return v;
 }
 
 // Order-preserving 32-bit code of an fp32 value for the argmax: NaN largest, -0 == +0.
@@ -163,42 +188,138 @@ __device__ __forceinline__ int pick_bin_warp(const uint32_t* hist, uint32_t need
   return bin;
 }
 
-__device__ __forceinline__ unsigned long long ld_cluster_u64(const void* local, uint32_t rank) {
-  unsigned long long v;
-  asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(mapa_shared(smem_u32(local), rank)) : "memory");
-  return v;
+// Order-preserving 32-bit codes of logits (NaN largest, -0 == +0) and their inverses
+// for non-NaN codes: fp16 bit patterns, fp32 values.
+__device__ __forceinline__ uint32_t code16(uint32_t h) {
+  if ((h & 0x7C00u) == 0x7C00u && (h & 0x03FFu) != 0u) return 0xFFFFu;
+  if (h == 0x8000u) h = 0u;
+  return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
+}
+__device__ __forceinline__ float decode16(uint32_t c) {
+  const uint32_t h = (c & 0x8000u) ? (c & 0x7FFFu) : (~c & 0xFFFFu);
+  return __half2float(__ushort_as_half(static_cast<uint16_t>(h)));
+}
+__device__ __forceinline__ float decode32(uint32_t c) { return __uint_as_float((c & 0x80000000u) ? (c & 0x7FFFFFFFu) : ~c); }
+
+// Codes of the eight columns [c, c + 8) (VEC: one or two 16-byte loads); columns at or
+// past `ce` get code 0, below every value.
+template <bool VEC>
+__device__ __forceinline__ void samp_codes8(const SampArgs& a, int64_t row, int c, int ce, uint32_t (&k)[8]) {
+  if (a.f32) {
+    float v[8];
+    if (VEC && c + 8 <= ce) {
+      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(a.logits) + row + c);
+      const float4 x = __ldg(p), y = __ldg(p + 1);
+      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+      v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = c + u < ce ? __ldg(static_cast<const float*>(a.logits) + row + c + u) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) k[u] = c + u < ce ? samp_code(v[u]) : 0u;
+  } else {
+    uint32_t h[8];
+    if (VEC && c + 8 <= ce) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.logits) + row + c));
+      h[0] = q.x & 0xFFFFu; h[1] = q.x >> 16; h[2] = q.y & 0xFFFFu; h[3] = q.y >> 16;
+      h[4] = q.z & 0xFFFFu; h[5] = q.z >> 16; h[6] = q.w & 0xFFFFu; h[7] = q.w >> 16;
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) h[u] = c + u < ce ? __ldg(static_cast<const uint16_t*>(a.logits) + row + c + u) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) k[u] = c + u < ce ? code16(h[u]) : 0u;
+  }
 }
 
-__device__ __forceinline__ uint32_t ld_cluster_u32(const void* local, uint32_t rank) {
-  uint32_t v;
-  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(mapa_shared(smem_u32(local), rank)) : "memory");
-  return v;
+__device__ __forceinline__ void st_cluster_u32(const void* local, uint32_t rank, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(mapa_shared(smem_u32(local), rank)), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_u64(const void* local, uint32_t rank, unsigned long long v) {
+  asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(mapa_shared(smem_u32(local), rank)), "l"(v) : "memory");
+}
+
+// First code in [lo, hi] at which the monotone predicate (true, ..., true, false, ...)
+// is false, given pred(hi) == false; 32 probes per round by one warp.
+template <typename Pred>
+__device__ __forceinline__ uint32_t warp_first_false(uint32_t lo, uint32_t hi, Pred pred) {
+  const int lane = threadIdx.x & 31;
+  while (lo < hi) {
+    const uint32_t stp = (hi - lo) / 31u + 1u;  // 31 steps reach past hi: lane 31 probes hi
+    const uint32_t c = min(hi, lo + static_cast<uint32_t>(lane) * stp);
+    const unsigned bal = __ballot_sync(0xffffffffu, !pred(c));
+    const int f = __ffs(bal) - 1;
+    const uint32_t cf = min(hi, lo + static_cast<uint32_t>(f) * stp);
+    if (f > 0) lo = min(hi, lo + static_cast<uint32_t>(f - 1) * stp) + 1u;
+    hi = cf;
+  }
+  return lo;
+}
+
+template <bool VEC>
+__device__ __forceinline__ void buf_load8(const uint16_t* buf, int o, int n, uint32_t (&w)[8]) {
+  if (VEC && o + 8 <= n) {
+    const uint4 q = *reinterpret_cast<const uint4*>(buf + o);
+    w[0] = q.x & 0xFFFFu; w[1] = q.x >> 16; w[2] = q.y & 0xFFFFu; w[3] = q.y >> 16;
+    w[4] = q.z & 0xFFFFu; w[5] = q.z >> 16; w[6] = q.w & 0xFFFFu; w[7] = q.w >> 16;
+  } else {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) w[u] = o + u < n ? buf[o + u] : 0xFFFFu;
+  }
+}
+
+template <bool VEC>
+__device__ __forceinline__ void buf_store8(uint16_t* buf, int o, int n, const uint32_t (&w)[8]) {
+  if (VEC && o + 8 <= n) {
+    *reinterpret_cast<uint4*>(buf + o) =
+        make_uint4(w[0] | (w[1] << 16), w[2] | (w[3] << 16), w[4] | (w[5] << 16), w[6] | (w[7] << 16));
+  } else {
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (o + u < n) buf[o + u] = static_cast<uint16_t>(w[u]);
+  }
 }
 
 // One cluster of gridDim.x CTAs per row (blockIdx.y); CTA r of the cluster owns the
-// contiguous columns [r * chunk, (r + 1) * chunk). Row-wide values are reduced through
-// distributed shared memory: each CTA publishes its partial in its own shared memory,
-// a cluster barrier, then every CTA (or the leader, rank 0) reads the partials of all
-// ranks in rank order. Every CTA of a cluster takes the same branches (they derive
-// from row-wide values), so all pass the same cluster barriers.
+// contiguous columns [r * chunk, (r + 1) * chunk) (chunk a multiple of 8). Row-wide
+// values are joined by pushing: each CTA stores its partial into a slot of every CTA
+// of the cluster (distributed shared memory), one cluster barrier, then every CTA
+// reduces the slots locally in rank order. Every CTA of a cluster takes the same
+// branches (they derive from row-wide values), so all pass the same cluster barriers,
+// and no CTA touches another's shared memory after the last barrier it passes.
+// Shared memory: the exp table, then the 16-bit column buffer of table indices (in the
+// row's global scratch when it does not fit).
+template <bool VEC>
 __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
-  extern __shared__ uint16_t ptab[];  // [size] fp16 probability bits per table index
+  extern __shared__ __align__(16) uint16_t ptab[];  // [size] the exp table, then the column buffer
   __shared__ unsigned long long red[kSampBlock / 32];
-  __shared__ unsigned long long part_a, part_b, bcast;
-  __shared__ uint32_t hist_c[256], hist_d[256], gh[256];
+  __shared__ unsigned long long xa[kSampMaxCluster], xb[kSampMaxCluster];  // pushed: max keys, sums
+  __shared__ unsigned long long xlist[kSampMaxCluster][kSampMaxK];  // pushed to the leader: sorted local top-k
+  __shared__ uint32_t xlen[kSampMaxCluster];
+  __shared__ uint32_t hist[256], hist2[256];  // high-bit, then low-bit histograms of this CTA's indices
   __shared__ uint32_t scan[kSampBlock / 32];
-  __shared__ unsigned long long lc[kSampMaxK], lt[kSampMaxK], cand[kSampMaxK], sorted[kSampMaxK];
-  __shared__ uint32_t lcn, ltn, lties;
-  __shared__ uint32_t gcnt[2 * 8 + 1];  // leader: per-rank candidate counts (> t, then ties) and their prefix
-  __shared__ uint32_t sel[4];  // bin, above, threshold, c_gt
+  __shared__ unsigned long long lc[kSampMaxK], sorted[kSampMaxK];
+  __shared__ unsigned long long bcast;
+  __shared__ uint32_t lcn, lties;
+  __shared__ uint32_t sel[4];  // histogram picks, then j_lo, j_hi and the fp16 bits of p(j_k)
   // the exp table into shared memory (it does not depend on the previous kernel, so
-  // this overlaps its tail); ptab holds table[j] until it becomes the probability table
+  // this overlaps its tail)
   if ((a.size & 7) == 0 && (reinterpret_cast<uintptr_t>(a.table) & 15) == 0) {
     for (int j = threadIdx.x; j < a.size / 8; j += kSampBlock)
       reinterpret_cast<uint4*>(ptab)[j] = __ldg(reinterpret_cast<const uint4*>(a.table) + j);
   } else {
     for (int j = threadIdx.x; j < a.size; j += kSampBlock) ptab[j] = __ldg(a.table + j);
   }
+  if (threadIdx.x == 0) {
+    lcn = 0;
+    lties = 0;
+  }
+  for (int b = threadIdx.x; b < 256; b += kSampBlock) {
+    hist[b] = 0;
+    hist2[b] = 0;
+  }
+  cluster_arrive_relaxed();  // phase 0: this CTA runs (awaited before the first remote store)
   pdl_wait();
   pdl_launch_dependents();
   const int C = static_cast<int>(gridDim.x);
@@ -206,51 +327,47 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
   const int n = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t row = static_cast<int64_t>(n) * a.V;
-  uint16_t* srow = a.scratch + row;
-  const int chunk = (a.V + C - 1) / C;
-  const int cb = min(a.V, static_cast<int>(r) * chunk), ce = min(a.V, cb + chunk);
-  if (tid == 0) {
-    lcn = 0;
-    ltn = 0;
-    lties = 0;
-  }
-  for (int b = tid; b < 256; b += kSampBlock) {
-    hist_c[b] = 0;
-    hist_d[b] = 0;
-  }
+  const int cb = min(a.V, static_cast<int>(r) * a.chunk), ce = min(a.V, cb + a.chunk);
+  const int nc = ce - cb;  // this CTA's columns
+  uint16_t* buf = a.buf_smem ? ptab + ((a.size + 7) & ~7) : a.scratch + row + cb;
 
-  // A: first index of the largest raw logit (NaN largest), row-wide
-  constexpr int kU = 8;  // loads issued before any is used
-  unsigned long long best = 0;
-  for (int base = cb + tid; base < ce; base += kU * kSampBlock) {
-    float v[kU];
+  // A: first index of the largest raw logit (NaN largest), row-wide, on the codes
+  uint32_t bcode = 0;
+  int bcol = -1;
+  for (int o = tid * 8; o < nc; o += kSampLd * 8 * kSampBlock) {  // kSampLd groups' loads in flight
+    uint32_t k8[kSampLd][8];
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int c = base + u * kSampBlock;
-      v[u] = c < ce ? samp_raw(a, row + c) : 0.0f;
-    }
+    for (int g = 0; g < kSampLd; ++g) samp_codes8<VEC>(a, row, cb + o + g * 8 * kSampBlock, ce, k8[g]);
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int c = base + u * kSampBlock;
-      const unsigned long long key =
-          (static_cast<unsigned long long>(samp_code(v[u])) << 32) | (0xFFFFFFFFull - c);
-      if (c < ce) best = key > best ? key : best;
-    }
+    for (int g = 0; g < kSampLd; ++g)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int oo = o + g * 8 * kSampBlock + u;
+        if (oo < nc && (bcol < 0 || k8[g][u] > bcode)) {  // columns ascend: strict > keeps the first
+          bcode = k8[g][u];
+          bcol = cb + oo;
+        }
+      }
   }
-  best = block_max_u64(best, red);  // its barriers also publish the staged table
-  if (tid == 0) part_a = best;
+  unsigned long long best =
+      bcol < 0 ? 0ull : (static_cast<unsigned long long>(bcode) << 32) | (0xFFFFFFFFull - static_cast<uint32_t>(bcol));
+  best = block_max_u64_w0(best, red);  // its barriers also publish the staged table
+  cluster_wait();                   // phase 0: every CTA of the cluster runs
+  if (tid < C) st_cluster_u64(&xa[r], tid, best);
   cluster_sync();
-  if (tid == 0) {
-    unsigned long long b = 0;
-    for (int q = 0; q < C; ++q) {
-      const unsigned long long v = ld_cluster_u64(&part_a, q);
-      b = v > b ? v : b;
+  if (tid < 32) {
+    unsigned long long v = lane < C ? xa[lane] : 0ull;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const unsigned long long x = __shfl_xor_sync(0xffffffffu, v, o);
+      v = x > v ? x : v;
     }
-    bcast = b;
+    if (tid == 0) bcast = v;
   }
   __syncthreads();
   best = bcast;
   const int amax = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+  const uint32_t acode = static_cast<uint32_t>(best >> 32);
   const float m = samp_scaled(a, samp_raw(a, row + amax));
   const uint32_t counter = *reinterpret_cast<volatile uint32_t*>(a.rng_state);
   const bool leader = r == 0;
@@ -261,33 +378,68 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
       a.logprobs[n] = __int_as_float(0x7fc00000);
     }
   } else {
-    // B: table indices and the exact sum of the table values, row-wide
-    unsigned long long acc = 0;
-    for (int base = cb + tid; base < ce; base += kU * kSampBlock) {
-      float v[kU];
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int c = base + u * kSampBlock;
-        v[u] = c < ce ? samp_raw(a, row + c) : 0.0f;
-      }
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int c = base + u * kSampBlock;
-        if (c < ce) {
-          const int j = samp_lut_index(samp_scaled(a, v[u]) - m, a.step, a.size);
-          if (a.scale) srow[c] = static_cast<uint16_t>(j);
-          const float e = __half2float(__ushort_as_half(ptab[a.size - 1 - j]));
-          acc += static_cast<unsigned long long>(e * 16777216.0f);  // exact: e is a multiple of 2^-24, <= 1
-        }
-      }
+    const int jclip = a.size - 1;
+    // Code -> index table for the highest codes up to the maximum (fp16 logits): j of a
+    // column is a non-increasing function of its code, so once the table's lowest code
+    // clips, every code below it clips too, and a column costs one compare or one
+    // lookup instead of two divisions. Codes below a table that does not reach the clip
+    // index (a flat row) take the exact path.
+    // The table grows downwards from the maximum in slices of one code per thread, and
+    // stops at the first slice whose lowest code clips (one slice for most rows).
+    const uint32_t lo_code = a.f32 ? 0x007FFFFFu : 0x03FFu;  // code of -inf
+    const uint32_t lmax = a.f32 ? 0u : min(acode - lo_code + 1u, static_cast<uint32_t>(min(a.lut_cap, kSampLutMax)));
+    uint16_t* cj = ptab + a.lut_off;  // cj[i]: index of code acode - i
+    uint32_t lw = 0;
+    bool below_clip = false;
+    while (lw < lmax && !below_clip) {  // CTA-uniform
+      const uint32_t i = lw + tid;
+      if (i < lmax) cj[i] = static_cast<uint16_t>(samp_lut_index(samp_scaled(a, decode16(acode - i)) - m, a.step, a.size));
+      lw = min(lmax, lw + kSampBlock);
+      __syncthreads();
+      below_clip = cj[lw - 1] == static_cast<uint16_t>(jclip);
     }
-    acc = block_sum_u64(acc, red);
-    if (tid == 0) part_b = acc;
+    const uint32_t lut_lo = acode + 1u - lw;  // lowest code of the table
+    // B: table indices and the exact sum of the table values (in units of 2^-24: every
+    // table value is a multiple of 2^-24, <= 1). With T > 0 the indices go to the column
+    // buffer, and the high bits of those below the clip index into this CTA's
+    // histogram, bin 255 - (j >> 7) (the bins of the smallest indices, the largest
+    // probabilities, come first).
+    unsigned long long acc = 0;
+    uint32_t nclip = 0;
+    for (int o = tid * 8; o < nc; o += 8 * kSampBlock) {
+      uint32_t k8[8], jw[8];
+      samp_codes8<VEC>(a, row, cb + o, ce, k8);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        int j = jclip;
+        if (o + u < nc) {
+          if (lw > 0 && k8[u] >= lut_lo) {
+            j = cj[acode - k8[u]];
+          } else if (!below_clip) {
+            const float x = a.f32 ? decode32(k8[u]) : decode16(k8[u]);
+            j = samp_lut_index(samp_scaled(a, x) - m, a.step, a.size);
+          }
+          if (j == jclip) {
+            ++nclip;
+          } else {
+            acc += static_cast<uint32_t>(__half2float(__ushort_as_half(ptab[a.size - 1 - j])) * 16777216.0f);
+            if (a.scale) atomicAdd(&hist[255 - (j >> 7)], 1u);
+          }
+        }
+        jw[u] = static_cast<uint32_t>(j);
+      }
+      if (a.scale) buf_store8<VEC>(buf, o, nc, jw);
+    }
+    acc += static_cast<unsigned long long>(nclip) *
+           static_cast<uint32_t>(__half2float(__ushort_as_half(ptab[0])) * 16777216.0f);
+    acc = block_sum_u64_w0(acc, red);  // its barriers also complete this CTA's histogram and indices
+    if (tid < C) st_cluster_u64(&xb[r], tid, acc);
     cluster_sync();
-    if (tid == 0) {
-      unsigned long long t = 0;
-      for (int q = 0; q < C; ++q) t += ld_cluster_u64(&part_b, q);
-      bcast = t;
+    if (tid < 32) {
+      unsigned long long v = lane < C ? xb[lane] : 0ull;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (tid == 0) bcast = v;
     }
     __syncthreads();
     float sum = __ull2float_rn(bcast) * 5.9604644775390625e-8f;  // * 2^-24, exact
@@ -300,183 +452,187 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
         a.logprobs[n] = __half2float(__float2half_rn(logf(p)));
       }
     } else {
-      // probability bits per table index, in place: ptab[j] = fp16(table[S-1-j] / sum)
-      // (entries j and S-1-j swap, one thread per pair)
-      for (int j = tid; j < (a.size + 1) / 2; j += kSampBlock) {
-        const int jj = a.size - 1 - j;
-        const float lo = __half2float(__ushort_as_half(ptab[j])), hi = __half2float(__ushort_as_half(ptab[jj]));
-        ptab[j] = __half_as_ushort(__float2half_rn(__fdiv_rn(hi, sum)));
-        ptab[jj] = __half_as_ushort(__float2half_rn(__fdiv_rn(lo, sum)));
-      }
-      __syncthreads();
+      // The probability of an element is p(j) = fp16(table[S-1-j] / sum) of its table
+      // index j alone, and p is non-increasing in j. The row's top-k by (p descending,
+      // column ascending) lies in the union of every CTA's own top-k by the same order,
+      // so each CTA selects its kl = min(k, columns) best columns locally (its k-th
+      // smallest index j_k, the indices [j_lo, j_hi] whose probability equals p(j_k),
+      // every column below j_lo and the first ties in column order), sorts them and
+      // pushes them to the leader, which ranks the union.
+      auto p16 = [&](int j) -> uint16_t {
+        return __half_as_ushort(
+            __float2half_rn(__fdiv_rn(__half2float(__ushort_as_half(ptab[a.size - 1 - j])), sum)));
+      };
       const uint32_t k = static_cast<uint32_t>(a.k);
-      // C: high byte histogram, row-wide
-      for (int base = cb; base < ce; base += kU * kSampBlock) {  // trip count uniform over the warp
-        uint32_t jv[kU];
+      const uint32_t kl = min(k, static_cast<uint32_t>(nc));
+      if (kl > 0) {  // CTA-uniform
+        // C, D: j_k from the high-bit histogram, then the low 7 bits inside its bin
+        if (tid < 32) {
+          uint32_t below = 0;
+          for (int i = lane; i < 256; i += 32) below += hist[i];
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int c = base + u * kSampBlock + tid;
-          jv[u] = c < ce ? __ldcg(srow + c) : 0xFFFFu;
-        }
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int bin = jv[u] != 0xFFFFu ? (ptab[jv[u]] >> 8) : -1;
-          const unsigned peers = __match_any_sync(0xffffffffu, bin);
-          if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist_c[bin], static_cast<uint32_t>(__popc(peers)));
-        }
-      }
-      __syncthreads();
-      cluster_sync();
-      if (tid < 256) {
-        uint32_t t = 0;
-        for (int q = 0; q < C; ++q) t += ld_cluster_u32(&hist_c[tid], q);
-        gh[tid] = t;
-      }
-      __syncthreads();
-      if (tid < 32) {
-        uint32_t above;
-        const int b = pick_bin_warp(gh, k, &above);
-        if (tid == 0) {
-          sel[0] = static_cast<uint32_t>(b);
-          sel[1] = above;
-        }
-      }
-      __syncthreads();
-      const uint32_t hb = sel[0], above_hi = sel[1];
-      // D: low byte histogram inside the high bin, row-wide
-      for (int base = cb; base < ce; base += kU * kSampBlock) {
-        uint32_t jv[kU];
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int c = base + u * kSampBlock + tid;
-          jv[u] = c < ce ? __ldcg(srow + c) : 0xFFFFu;
-        }
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          int bin = -1;
-          if (jv[u] != 0xFFFFu) {
-            const uint32_t p = ptab[jv[u]];
-            if ((p >> 8) == hb) bin = static_cast<int>(p & 0xFFu);
-          }
-          const unsigned peers = __match_any_sync(0xffffffffu, bin);
-          if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist_d[bin], static_cast<uint32_t>(__popc(peers)));
-        }
-      }
-      __syncthreads();
-      cluster_sync();
-      if (tid < 256) {
-        uint32_t t = 0;
-        for (int q = 0; q < C; ++q) t += ld_cluster_u32(&hist_d[tid], q);
-        gh[tid] = t;
-      }
-      __syncthreads();
-      if (tid < 32) {
-        uint32_t above;
-        const int lo = pick_bin_warp(gh, k - above_hi, &above);
-        if (tid == 0) {
-          sel[2] = (hb << 8) | static_cast<uint32_t>(lo);
-          sel[3] = above_hi + above;
-        }
-      }
-      __syncthreads();
-      const uint32_t t = sel[2], c_gt = sel[3];
-      const uint32_t need = k - c_gt;  // >= 1 columns with p == t, the first ones by column
-      // E: contiguous column range per thread inside this CTA's range, in column order
-      const int sub = (ce - cb + kSampBlock - 1) / kSampBlock;
-      const int c0 = min(ce, cb + tid * sub), c1 = min(ce, c0 + sub);
-      uint32_t ties = 0;
-      for (int cc = c0; cc < c1; cc += kU) {
-        uint32_t jv[kU];
-#pragma unroll
-        for (int u = 0; u < kU; ++u) jv[u] = cc + u < c1 ? __ldcg(srow + cc + u) : 0u;
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int c = cc + u;
-          if (c >= c1) break;
-          const uint32_t p = ptab[jv[u]];
-          if (p > t) {
-            const uint32_t slot = atomicAdd(&lcn, 1u);
-            if (slot < kSampMaxK) lc[slot] = (static_cast<unsigned long long>(p) << 32) | (0xFFFFFFFFull - c);
-          } else if (p == t) {
-            ++ties;
+          for (int o = 16; o; o >>= 1) below += __shfl_xor_sync(0xffffffffu, below, o);
+          uint32_t above = 0;
+          const int b = below >= kl ? pick_bin_warp(hist, kl, &above) : -1;
+          if (tid == 0) {
+            sel[0] = static_cast<uint32_t>(b);
+            sel[1] = above;
           }
         }
-      }
-      // exclusive prefix of the tie counts over threads (thread order = column order)
-      uint32_t incl = ties;
+        __syncthreads();
+        int jk = jclip;
+        if (static_cast<int>(sel[0]) >= 0) {
+          const int hb = 255 - static_cast<int>(sel[0]);
+          const uint32_t above_hi = sel[1];
+          for (int o = tid * 8; o < nc; o += 8 * kSampBlock) {
+            uint32_t jv[8];
+            buf_load8<VEC>(buf, o, nc, jv);
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += x;
-      }
-      if (lane == 31) scan[tid >> 5] = incl;
-      __syncthreads();
-      if (tid < 32) {
-        const uint32_t v = scan[tid];
-        uint32_t s2 = v;
+            for (int u = 0; u < 8; ++u) {
+              const int j = static_cast<int>(jv[u]);
+              if (jv[u] != 0xFFFFu && j != jclip && (j >> 7) == hb) atomicAdd(&hist2[255 - (j & 127)], 1u);
+            }
+          }
+          __syncthreads();
+          if (tid < 32) {
+            uint32_t above;
+            const int lo = pick_bin_warp(hist2, kl - above_hi, &above);
+            if (tid == 0) sel[2] = static_cast<uint32_t>((hb << 7) | (255 - lo));
+          }
+          __syncthreads();
+          jk = static_cast<int>(sel[2]);
+        }
+        __syncthreads();  // every thread has read j_k before sel[] is reused
+        // [j_lo, j_hi]: two 32-way searches of the monotone p, one warp each
+        if (tid < 64) {
+          const float pk = __half2float(__ushort_as_half(p16(jk)));
+          if (tid < 32) {  // j_lo: first j in [0, j_k] with p(j) <= p(j_k)
+            const uint32_t f = warp_first_false(0u, static_cast<uint32_t>(jk), [&](uint32_t j) {
+              return __half2float(__ushort_as_half(p16(static_cast<int>(j)))) > pk;
+            });
+            if (tid == 0) sel[2] = f;
+          } else {  // j_hi + 1: first j in [j_k, size] with p(j) < p(j_k) (size: past the table)
+            const uint32_t f = warp_first_false(static_cast<uint32_t>(jk), static_cast<uint32_t>(a.size), [&](uint32_t j) {
+              return static_cast<int>(j) < a.size && __half2float(__ushort_as_half(p16(static_cast<int>(j)))) >= pk;
+            });
+            if (tid == 32) {
+              sel[3] = f - 1u;
+              sel[1] = p16(jk);
+            }
+          }
+        }
+        __syncthreads();
+        const int jlo = static_cast<int>(sel[2]), jhi = static_cast<int>(sel[3]);
+        const uint32_t t = sel[1];  // fp16 bits of p(j_k)
+        // E: contiguous column ranges of whole 8-column groups per thread, in column order
+        const int sub = (((nc + kSampBlock - 1) / kSampBlock) + 7) & ~7;
+        const int o0 = min(nc, tid * sub), o1 = min(nc, o0 + sub);
+        uint32_t ties = 0;
+        for (int o = o0; o < o1; o += 8) {
+          uint32_t jv[8];
+          buf_load8<VEC>(buf, o, o1, jv);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            if (o + u >= o1) break;
+            const int j = static_cast<int>(jv[u]);
+            if (j < jlo) {  // p(j) > p(j_k): fewer than kl such columns here
+              const uint32_t slot = atomicAdd(&lcn, 1u);
+              if (slot < kSampMaxK)
+                lc[slot] = (static_cast<unsigned long long>(p16(j)) << 32) | (0xFFFFFFFFull - (cb + o + u));
+            } else if (j <= jhi) {  // p(j) == p(j_k)
+              ++ties;
+            }
+          }
+        }
+        // exclusive prefix of the tie counts over threads (thread order = column order)
+        uint32_t incl = ties;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t x = __shfl_up_sync(0xffffffffu, s2, o);
-          if (lane >= o) s2 += x;
+          const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += x;
         }
-        scan[tid] = s2 - v;  // exclusive over warps
-        if (tid == 31) lties = s2;  // this CTA's tie count
-      }
-      __syncthreads();
-      cluster_sync();  // tie counts of every rank published
-      if (tid == 0) {
-        uint32_t off = 0;
-        for (uint32_t q = 0; q < r; ++q) off += ld_cluster_u32(&lties, q);
-        sel[0] = off;  // ties in lower ranks' columns
-        ltn = off >= need ? 0u : min(lties, need - off);
-      }
-      __syncthreads();
-      const uint32_t lim = ltn;
-      uint32_t rank = scan[tid >> 5] + incl - ties;  // local rank among this CTA's ties
-      for (int cc = c0; cc < c1 && ties > 0 && rank < lim; cc += kU) {
-        uint32_t jv[kU];
-#pragma unroll
-        for (int u = 0; u < kU; ++u) jv[u] = cc + u < c1 ? __ldcg(srow + cc + u) : 0u;
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int c = cc + u;
-          if (c < c1 && rank < lim && ptab[jv[u]] == t) {
-            lt[rank] = (static_cast<unsigned long long>(t) << 32) | (0xFFFFFFFFull - c);
-            ++rank;
-          }
-        }
-      }
-      __syncthreads();
-      cluster_sync();  // candidate lists of every rank published
-      if (leader) {
-        // gather the ranks' lists: counts first (one thread per list), then one
-        // thread per candidate, so the remote loads overlap
-        if (tid < 2 * C) {
-          const int q = tid % C;
-          gcnt[tid] = tid < C ? min(ld_cluster_u32(&lcn, q), static_cast<uint32_t>(kSampMaxK))
-                              : ld_cluster_u32(&ltn, q);
-        }
+        if (lane == 31) scan[tid >> 5] = incl;
         __syncthreads();
-        if (tid < static_cast<int>(k)) {
-          uint32_t i = static_cast<uint32_t>(tid), list = 0;
-          while (list < static_cast<uint32_t>(2 * C) && i >= gcnt[list]) i -= gcnt[list++];
-          unsigned long long key = 0;  // unreachable zero when the counts agree
-          if (list < static_cast<uint32_t>(2 * C)) {
-            const uint32_t q = list % C;
-            key = list < static_cast<uint32_t>(C) ? ld_cluster_u64(&lc[i], q) : ld_cluster_u64(&lt[i], q);
-          }
-          cand[tid] = key;
-        }
-        __syncthreads();
-        // rank the k candidate keys (distinct: the column is part of the key)
         if (tid < 32) {
-          for (uint32_t i = tid; i < k; i += 32) {
-            const unsigned long long key = cand[i];
-            uint32_t rk = 0;
-            for (uint32_t j = 0; j < k; ++j) rk += cand[j] > key ? 1u : 0u;
-            sorted[rk] = key;
+          const uint32_t v = scan[tid];
+          uint32_t s2 = v;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t x = __shfl_up_sync(0xffffffffu, s2, o);
+            if (lane >= o) s2 += x;
+          }
+          scan[tid] = s2 - v;  // exclusive over warps
+        }
+        __syncthreads();
+        const uint32_t c_gt = min(lcn, kl);       // < kl by construction
+        const uint32_t need = kl - c_gt;          // ties to take, the first ones by column
+        uint32_t rank = scan[tid >> 5] + incl - ties;  // rank among this CTA's ties
+        for (int o = o0; o < o1 && ties > 0 && rank < need; o += 8) {
+          uint32_t jv[8];
+          buf_load8<VEC>(buf, o, o1, jv);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            if (o + u < o1 && rank < need && static_cast<int>(jv[u]) >= jlo && static_cast<int>(jv[u]) <= jhi) {
+              lc[c_gt + rank] = (static_cast<unsigned long long>(t) << 32) | (0xFFFFFFFFull - (cb + o + u));
+              ++rank;
+            }
           }
         }
+        __syncthreads();
+        // this CTA's kl keys, sorted (descending, distinct: the column is part of the
+        // key), into the leader's list of this rank
+        if (tid < static_cast<int>(kl)) {
+          const unsigned long long key = lc[tid];
+          uint32_t rk = 0;
+          for (uint32_t i = 0; i < kl; ++i) rk += lc[i] > key ? 1u : 0u;
+          st_cluster_u64(&xlist[r][rk], 0, key);
+        }
+      }
+      if (tid == 0) st_cluster_u32(&xlen[r], 0, kl);
+      cluster_sync();  // the leader holds every rank's sorted list
+      if (leader) {
+        // Merge the sorted lists pairwise, keeping the k largest keys of every merge: a
+        // key's place in the merge is its place in its own list plus the number of
+        // larger keys in the partner list (binary search; keys are distinct). Scratch:
+        // the code table's space, free by now (at least 2 x 8 x 64 keys).
+        unsigned long long* mbuf = reinterpret_cast<unsigned long long*>(ptab + a.lut_off);
+        const unsigned long long* src = &xlist[0][0];
+        const uint32_t* slen = xlen;
+        __shared__ uint32_t mlen[2][kSampMaxCluster / 2];
+        int lists = C, level = 0;
+        while (lists > 1) {  // CTA-uniform
+          unsigned long long* dst = mbuf + (level & 1) * (kSampMaxCluster / 2) * kSampMaxK;
+          uint32_t* dlen = mlen[level & 1];
+          const int L = tid / kSampMaxK, i = tid % kSampMaxK;
+          if (L < lists && i < static_cast<int>(slen[L])) {
+            const unsigned long long x = src[L * kSampMaxK + i];
+            const int P = L ^ 1;
+            uint32_t lo = 0;
+            if (P < lists) {
+              const unsigned long long* pl = src + P * kSampMaxK;
+              uint32_t hi = slen[P];
+              while (lo < hi) {
+                const uint32_t mid = (lo + hi) >> 1;
+                if (pl[mid] > x)
+                  lo = mid + 1;
+                else
+                  hi = mid;
+              }
+            }
+            const uint32_t rk = static_cast<uint32_t>(i) + lo;
+            if (rk < k) dst[(L >> 1) * kSampMaxK + rk] = x;
+          }
+          if (tid < (lists + 1) / 2) {
+            const uint32_t l0 = slen[2 * tid], l1 = 2 * tid + 1 < lists ? slen[2 * tid + 1] : 0u;
+            dlen[tid] = min(k, l0 + l1);
+          }
+          __syncthreads();
+          src = dst;
+          slen = dlen;
+          lists = (lists + 1) / 2;
+          ++level;
+        }
+        if (tid < static_cast<int>(k)) sorted[tid] = src[tid];
         __syncthreads();
         if (tid == 0) {
           float u;
@@ -488,18 +644,36 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
             u = static_cast<float>(splitmix64(base + static_cast<unsigned long long>(n)) >> 40) *
                 5.9604644775390625e-8f;
           }
+          // fp32 running sums in candidate order (eight loads in flight, then the adds)
           float total = 0.0f;
-          for (uint32_t i = 0; i < k; ++i)
-            total += __half2float(__ushort_as_half(static_cast<uint16_t>(sorted[i] >> 32)));
+          for (uint32_t i0 = 0; i0 < k; i0 += 8) {
+            float pv[8];
+#pragma unroll
+            for (uint32_t q = 0; q < 8; ++q)
+              pv[q] = i0 + q < k ? __half2float(__ushort_as_half(static_cast<uint16_t>(sorted[i0 + q] >> 32))) : 0.0f;
+#pragma unroll
+            for (uint32_t q = 0; q < 8; ++q)
+              if (i0 + q < k) total += pv[q];
+          }
           uint32_t pick = k - 1;
           if (total > 0.0f) {
             const float target = u * total;
             float run = 0.0f;
-            for (uint32_t i = 0; i < k; ++i) {
-              run += __half2float(__ushort_as_half(static_cast<uint16_t>(sorted[i] >> 32)));
-              if (run > target) {
-                pick = i;
-                break;
+            bool found = false;
+            for (uint32_t i0 = 0; i0 < k && !found; i0 += 8) {
+              float pv[8];
+#pragma unroll
+              for (uint32_t q = 0; q < 8; ++q)
+                pv[q] = i0 + q < k ? __half2float(__ushort_as_half(static_cast<uint16_t>(sorted[i0 + q] >> 32))) : 0.0f;
+#pragma unroll
+              for (uint32_t q = 0; q < 8; ++q) {
+                if (!found && i0 + q < k) {
+                  run += pv[q];
+                  if (run > target) {
+                    pick = i0 + q;
+                    found = true;
+                  }
+                }
               }
             }
           } else {
@@ -513,8 +687,6 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
       }
     }
   }
-  // no CTA leaves while the leader may still read its shared memory
-  cluster_sync();
   // the last row's leader advances the random stream's counter (read by the next call)
   if (leader && tid == 0) {
     __threadfence();
@@ -525,37 +697,44 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
     }
   }
 }
-
 }  // namespace mb
 
 using namespace mb;
 
 // Per device, once: the kernel's shared-memory limit and how many clusters of each
-// size (1 CTA of 1024 threads and 64 KB + static shared memory per SM) fit at once.
+// size (1 CTA of 1024 threads per SM; sizes above 8 are non-portable) fit at once.
 constexpr int kSampMaxDevices = 64;
+constexpr size_t kSampSmemMax = 200 * 1024;  // dynamic: the table, column buffer and code table
 struct SampDevice {
   bool ready = false;
-  int capacity[9] = {};
+  int capacity[kSampMaxCluster + 1] = {};
 };
 static SampDevice g_samp_dev[kSampMaxDevices];
 static std::once_flag g_samp_once[kSampMaxDevices];
 
+template <bool VEC>
+static bool samp_attrs() {
+  if (cudaFuncSetAttribute(k_sample<VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kSampSmemMax)) != cudaSuccess ||
+      cudaFuncSetAttribute(k_sample<VEC>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return true;
+}
+
 static SampDevice& samp_device(int dev) {
   std::call_once(g_samp_once[dev], [dev] {
     SampDevice& sd = g_samp_dev[dev];
-    const int smem = 32768 * static_cast<int>(sizeof(uint16_t));
-    if (cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
-      (void)cudaGetLastError();
-      return;
-    }
+    if (!samp_attrs<true>() || !samp_attrs<false>()) return;
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     sd.capacity[1] = sms;
-    for (int c = 2; c <= 8; ++c) {
+    for (int c = 2; c <= kSampMaxCluster; ++c) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(c, 1);
       cfg.blockDim = dim3(kSampBlock);
-      cfg.dynamicSmemBytes = smem;
+      cfg.dynamicSmemBytes = kSampSmemMax;
       cudaLaunchAttribute attr;
       attr.id = cudaLaunchAttributeClusterDimension;
       attr.val.clusterDim.x = c;
@@ -564,7 +743,7 @@ static SampDevice& samp_device(int dev) {
       cfg.attrs = &attr;
       cfg.numAttrs = 1;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, k_sample, &cfg) != cudaSuccess) {
+      if (cudaOccupancyMaxActiveClusters(&n, k_sample<true>, &cfg) != cudaSuccess) {
         (void)cudaGetLastError();
         n = 0;
       }
@@ -602,6 +781,9 @@ int32_t mb_sample_tokens(const void* logits, int32_t logits_f32, int32_t N, int3
   a.table = table;
   a.size = size;
   a.step = static_cast<float>(static_cast<double>(range_max) / (size - 1));
+  // a >= clip gives a / step > size - 1 in real numbers, so the fp32 quotient rounds to
+  // at least size - 1 (representable) and the index clips: no division needed
+  a.clip = static_cast<float>(static_cast<double>(size - 1) * static_cast<double>(a.step) * (1.0 + 0x1p-20));
   a.uniforms = uniforms;
   a.seed = seed;
   a.rng_state = rng_state;
@@ -609,7 +791,6 @@ int32_t mb_sample_tokens(const void* logits, int32_t logits_f32, int32_t N, int3
   a.logprobs = logprobs;
   a.scratch = static_cast<uint16_t*>(workspace);
   a.err = dev_err;
-  const size_t smem = static_cast<size_t>(size) * sizeof(uint16_t);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kSampMaxDevices) {
     (void)cudaGetLastError();
@@ -617,13 +798,25 @@ int32_t mb_sample_tokens(const void* logits, int32_t logits_f32, int32_t N, int3
   }
   SampDevice& sd = samp_device(dev);
   if (!sd.ready) return MB_ERR_LAUNCH;
-  // cluster size: the largest C <= 8 whose N clusters are resident at once (one wave)
+  // cluster size: the largest C <= 16 whose N clusters are resident at once (one wave)
   int C = 1;
-  for (int c = 8; c >= 2; --c)
+  for (int c = kSampMaxCluster; c >= 2; --c)
     if (sd.capacity[c] >= N) {
       C = c;
       break;
     }
+  a.chunk = static_cast<int>((((static_cast<int64_t>(V) + C - 1) / C) + 7) / 8 * 8);
+  const size_t tab_bytes = static_cast<size_t>((size + 7) & ~7) * sizeof(uint16_t);
+  // the code table's space doubles as the leader's merge scratch: keep at least 8 KB
+  a.buf_smem = tab_bytes + static_cast<size_t>(a.chunk) * sizeof(uint16_t) + 8192 <= kSampSmemMax ? 1 : 0;
+  // the rest of the budget holds the code -> index table (up to every fp16 code)
+  a.lut_off = static_cast<int>(tab_bytes / sizeof(uint16_t)) + (a.buf_smem ? a.chunk : 0);
+  a.lut_cap = std::min(65536, static_cast<int>(kSampSmemMax / sizeof(uint16_t)) - a.lut_off) & ~7;
+  if (a.lut_cap < 0) a.lut_cap = 0;
+  const size_t smem = (static_cast<size_t>(a.lut_off) + a.lut_cap) * sizeof(uint16_t);
+  // 16-byte loads of whole 8-column groups: every row and chunk starts 16-byte aligned
+  const bool vec = V % 8 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(workspace) & 15) == 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(C, N);
   cfg.blockDim = dim3(kSampBlock);
@@ -638,7 +831,8 @@ int32_t mb_sample_tokens(const void* logits, int32_t logits_f32, int32_t N, int3
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  if (cudaLaunchKernelEx(&cfg, k_sample, a) != cudaSuccess) {
+  if ((vec ? cudaLaunchKernelEx(&cfg, k_sample<true>, a) : cudaLaunchKernelEx(&cfg, k_sample<false>, a)) !=
+      cudaSuccess) {
     (void)cudaGetLastError();
     return MB_ERR_LAUNCH;
   }

@@ -92,6 +92,23 @@ def test_big_vocabulary_and_ties(cuda):
     assert 0 <= tok[1] < 50 and 0 <= tok[2] < 50
 
 
+@pytest.mark.parametrize("T", [100.0, 0.05])
+def test_big_vocabulary_plateaus_and_clipped_rows(cuda, T):
+    """Full config-5 rows at the two ends of the temperature range. T = 100: every
+    probability is about 1/V, in the fp16 subnormal range, where long runs of
+    neighbouring table indices share one probability (the tie interval of the k-th
+    largest spans many indices). T = 0.05: fewer than 50 columns lie within the table's
+    range of the maximum, so the set is completed with the first columns at the clipped
+    index."""
+    x = S.make_logits(4, 151936, 12, 3.0, np.float16)
+    u = np.array([0.1, 0.5, 0.9, 0.0], np.float32)
+    tok, lp, err = _run(x, T, cuda, uniforms=u)
+    otok, olp = S.sample_tokens(x, T, TABLE, 10.0, u)
+    assert err == 0
+    np.testing.assert_array_equal(tok, otok)
+    np.testing.assert_allclose(lp, olp, rtol=1e-6, atol=1e-6)
+
+
 @pytest.mark.parametrize("V", [1, 7, 50, 63, 1000])
 def test_small_vocabularies(cuda, V):
     x = S.make_logits(3, V, 4, 2.0, np.float32)
