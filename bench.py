@@ -16,7 +16,8 @@ reported beside it. The GEMM launches of a step are replayed from a CUDA graph.
 
 ``e2e`` measures the same sweep through the public Python API (``batched_gemm``) as a
 host user calls it: per call the activations come from pinned host memory and the
-output goes back to pinned host memory, one synchronise per step.
+output goes back to pinned host memory (the copies overlap the neighbouring calls'
+kernels on the library's copy streams), one host wait per step.
 
 ``--impl reference`` times the reference's CPU path (the NumPy oracle port of
 src/dequant.py:116-147 + the fp32 CPU GEMM of test_batched_speed.py:39-42) on this
@@ -855,7 +856,7 @@ def run_e2e(args, dev, stream, shard, sweep, Ms, world, rank, bounds, R):
     import torch
     import torch.distributed as dist
     from moat_b200.dist import gather_columns
-    from moat_b200.gemm import batched_gemm
+    from moat_b200.gemm import batched_gemm, host_wait
 
     K, M = K_DIM, M_DIM
     R_e = min(R, args.e2e_ring)
@@ -878,6 +879,8 @@ def run_e2e(args, dev, stream, shard, sweep, Ms, world, rank, bounds, R):
                     dev_x[n].copy_(host_x[n], non_blocking=True)
                     y = gather_columns(batched_gemm(dev_x[n], ring[r], K, Ms), bounds)
                     host_y[n][r].copy_(y, non_blocking=True)
+            if world == 1:
+                host_wait(dev)  # the copies of the host calls run on the library's copy streams
             stream.synchronize()
 
     for _ in range(max(1, args.warmup)):
@@ -899,8 +902,9 @@ def run_e2e(args, dev, stream, shard, sweep, Ms, world, rank, bounds, R):
             "d2h_bytes_per_step": d2h, "steps": steps, "calls_per_step": R_e * len(sweep),
             "tok_per_s": sum(sweep) * R_e * steps / el,
             "how": "public API batched_gemm per call with pinned host activations and output (1 GPU: "
-                   "one C call per GEMM does the H2D copy, the kernel and the D2H copy; N GPUs: H2D, "
-                   "kernel, all-gather, D2H); wall clock around steps, one synchronise per step"}
+                   "one C call per GEMM enqueues the H2D copy, the kernel and the D2H copy, the copies "
+                   "on library copy streams so that they overlap the neighbouring calls' kernels; N GPUs: "
+                   "H2D, kernel, all-gather, D2H); wall clock around steps, one host wait per step"}
 
 
 def main():

@@ -125,6 +125,23 @@ int32_t mb_int4_gemm(const uint16_t* act, const uint8_t* sb, uint16_t* out, int3
 int32_t mb_int4_gemm_host(const uint16_t* act_host, const uint8_t* sb, uint16_t* out_host, int32_t N, int32_t K,
                           int32_t M, uint16_t* act_dev, uint16_t* out_dev, uint32_t* dev_err, void* stream);
 
+/* Host-buffer GEMM for a stream of calls (the same flow as mb_int4_gemm_host, without
+ * its serialisation): the input copy and the output copy of each call run on two
+ * library-owned copy streams, ordered with events against `stream` (which runs the
+ * GEMM), and each call uses the next of MB_HOST_SLOTS staging slots of `staging`
+ * (256-byte aligned, staging_bytes / MB_HOST_SLOTS bytes per slot, at least
+ * mb_int4_gemm_host_staging_bytes(N, K, M) / MB_HOST_SLOTS), so consecutive calls'
+ * copies overlap their neighbours' GEMMs. Returns once enqueued: out_host is complete,
+ * and act_host may be reused, after mb_int4_gemm_host_wait(stream) (or a device
+ * synchronise). A slot is rewritten only after its previous output copy finished. */
+#define MB_HOST_SLOTS 4
+size_t mb_int4_gemm_host_staging_bytes(int32_t N, int32_t K, int32_t M);
+int32_t mb_int4_gemm_host_overlap(const uint16_t* act_host, const uint8_t* sb, uint16_t* out_host, int32_t N,
+                                  int32_t K, int32_t M, void* staging, size_t staging_bytes, uint32_t* dev_err,
+                                  void* stream);
+/* Wait on the host for every mb_int4_gemm_host_overlap call enqueued for `stream`. */
+int32_t mb_int4_gemm_host_wait(void* stream);
+
 /* Launch plan of the first 32-row block for a shape (introspection, no reference
  * counterpart). info must hold 8 int32: [0] fast path (1) or generic (0), [1] strip
  * width, [2] CTAs per cluster (K split), [3] grid size, [4] pipeline stages, [5]

@@ -29,6 +29,9 @@ SIGNATURES = {
     "mb_lut_gather_f16": (_c_i32, [_vp, _c_i64, _vp, _c_i64, _c_i32, _c_i64, _vp, _vp]),
     "mb_int4_gemm": (_c_i32, [_vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _vp, _vp]),
     "mb_int4_gemm_host": (_c_i32, [_vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _vp, _vp, _vp, _vp]),
+    "mb_int4_gemm_host_staging_bytes": (_c_sz, [_c_i32, _c_i32, _c_i32]),
+    "mb_int4_gemm_host_overlap": (_c_i32, [_vp, _vp, _vp, _c_i32, _c_i32, _c_i32, _vp, _c_sz, _vp, _vp]),
+    "mb_int4_gemm_host_wait": (_c_i32, [_vp]),
     "mb_int4_gemm_plan": (_c_i32, [_c_i32, _c_i32, _c_i32, ctypes.POINTER(_c_i32)]),
     "mb_int4_extract_columns": (_c_i32, [_vp, _c_i32, _c_i32, _c_i32, _c_i32, _vp, _vp]),
     "mb_exp_lut_lookup": (_c_i32, [_vp, _c_i32, _c_f, _vp, _c_i64, _vp, _vp]),

@@ -964,6 +964,100 @@ int32_t mb_int4_gemm_host(const uint16_t* act_host, const uint8_t* sb, uint16_t*
   return MB_OK;
 }
 
+// Host-buffer calls that overlap one another: per (device, caller stream) a pipe of two
+// library-owned copy streams and MB_HOST_SLOTS staging slots. Call i copies its input
+// into slot i % MB_HOST_SLOTS on the input stream, the caller's stream waits for that
+// copy and runs the GEMM, and the output stream waits for the GEMM and copies the
+// result out; each slot's next input copy waits for its previous output copy. So the
+// input copy of the next call and the output copy of the previous one run beside
+// the current GEMM (separate copy engines), and no slot is overwritten while in use.
+constexpr int kHostSlots = MB_HOST_SLOTS;
+struct HostPipe {
+  cudaStream_t s_in = nullptr, s_out = nullptr;
+  cudaEvent_t ev_in[kHostSlots] = {}, ev_k[kHostSlots] = {}, ev_out[kHostSlots] = {};
+  uint32_t next = 0;
+};
+
+static HostPipe* host_pipe(cudaStream_t st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return nullptr;
+  }
+  const uint64_t key = (static_cast<uint64_t>(dev & 0xFF) << 56) ^ static_cast<uint64_t>(reinterpret_cast<uintptr_t>(st));
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, HostPipe*> pipes;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = pipes.find(key);
+  if (it != pipes.end()) return it->second;
+  HostPipe* p = new HostPipe();
+  bool ok = cudaStreamCreateWithFlags(&p->s_in, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&p->s_out, cudaStreamNonBlocking) == cudaSuccess;
+  for (int i = 0; ok && i < kHostSlots; ++i)
+    ok = cudaEventCreateWithFlags(&p->ev_in[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&p->ev_k[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&p->ev_out[i], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
+    (void)cudaGetLastError();
+    return nullptr;  // leaked on failure: a process that cannot create streams has bigger problems
+  }
+  pipes.emplace(key, p);
+  return p;
+}
+
+static inline size_t host_slot_in(int32_t N, int32_t K) { return (static_cast<size_t>(N) * K * 2 + 255) / 256 * 256; }
+static inline size_t host_slot_bytes(int32_t N, int32_t K, int32_t M) {
+  return host_slot_in(N, K) + (static_cast<size_t>(N) * M * 2 + 255) / 256 * 256;
+}
+
+size_t mb_int4_gemm_host_staging_bytes(int32_t N, int32_t K, int32_t M) {
+  if (N < 1 || K < 1 || M < 1) return 0;
+  return static_cast<size_t>(kHostSlots) * host_slot_bytes(N, K, M);
+}
+
+int32_t mb_int4_gemm_host_overlap(const uint16_t* act_host, const uint8_t* sb, uint16_t* out_host, int32_t N,
+                                  int32_t K, int32_t M, void* staging, size_t staging_bytes, uint32_t* dev_err,
+                                  void* stream) {
+  if (!act_host || !sb || !out_host || !staging) return MB_ERR_NULL;
+  if (N < 1 || K < 1 || M < 1 || (static_cast<int64_t>(K) * M) % 256 != 0) return MB_ERR_ARGS;
+  if (!aligned(staging, 256)) return MB_ERR_ALIGN;
+  const size_t slot = (staging_bytes / kHostSlots) / 256 * 256;  // slots of a fixed size whatever the shape
+  if (host_slot_bytes(N, K, M) > slot) return MB_ERR_WORKSPACE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  HostPipe* p = host_pipe(st);
+  if (!p) return MB_ERR_LAUNCH;
+  const int s = static_cast<int>(p->next++ % kHostSlots);
+  uint8_t* base = static_cast<uint8_t*>(staging) + static_cast<size_t>(s) * slot;
+  uint16_t* in = reinterpret_cast<uint16_t*>(base);
+  uint16_t* out = reinterpret_cast<uint16_t*>(base + host_slot_in(N, K));
+  const size_t in_bytes = static_cast<size_t>(N) * K * 2, out_bytes = static_cast<size_t>(N) * M * 2;
+  if (cudaStreamWaitEvent(p->s_in, p->ev_out[s], 0) != cudaSuccess ||
+      cudaMemcpyAsync(in, act_host, in_bytes, cudaMemcpyHostToDevice, p->s_in) != cudaSuccess ||
+      cudaEventRecord(p->ev_in[s], p->s_in) != cudaSuccess || cudaStreamWaitEvent(st, p->ev_in[s], 0) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return MB_ERR_LAUNCH;
+  }
+  const int32_t rc = gemm_all(in, sb, out, N, K, M, dev_err, stream);
+  if (rc != MB_OK) return rc;
+  if (cudaEventRecord(p->ev_k[s], st) != cudaSuccess || cudaStreamWaitEvent(p->s_out, p->ev_k[s], 0) != cudaSuccess ||
+      cudaMemcpyAsync(out_host, out, out_bytes, cudaMemcpyDeviceToHost, p->s_out) != cudaSuccess ||
+      cudaEventRecord(p->ev_out[s], p->s_out) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return MB_ERR_LAUNCH;
+  }
+  return MB_OK;
+}
+
+int32_t mb_int4_gemm_host_wait(void* stream) {
+  HostPipe* p = host_pipe(static_cast<cudaStream_t>(stream));
+  if (!p) return MB_ERR_LAUNCH;
+  if (cudaStreamSynchronize(p->s_in) != cudaSuccess || cudaStreamSynchronize(p->s_out) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return MB_ERR_LAUNCH;
+  }
+  return MB_OK;
+}
+
 int32_t mb_int4_gemm_plan(int32_t N, int32_t K, int32_t M, int32_t* info) {
   if (!info) return MB_ERR_NULL;
   if (N < 1 || K < 1 || M < 1) return MB_ERR_ARGS;

@@ -41,10 +41,11 @@ def batched_gemm(activations, superblocks, K: int, M: int, out=None, dev_err=Non
     int32 CUDA tensor whose first word receives device error bits (bounded waits).
 
     Host path: with CPU torch ``activations`` and a CPU torch ``out`` (pinned memory
-    for asynchronous copies) and the weights on a GPU, one C call copies the
-    activations in, runs the GEMM and copies the result back on the current stream
-    (``mb_int4_gemm_host``); with ``sync=False`` it returns without waiting and the
-    caller synchronises the stream before reading ``out``.
+    for asynchronous copies) and the weights on a GPU, one C call enqueues the copy in,
+    the GEMM (on the current stream) and the copy back (``mb_int4_gemm_host_overlap``:
+    the copies run on library streams, so consecutive calls' copies overlap their
+    neighbours' GEMMs); with ``sync=False`` it returns at once, and ``out`` is complete
+    (and ``activations`` free to change) after ``host_wait()`` or a device synchronise.
     """
     t = _lib.torch()
     if type(activations) is t.Tensor and type(superblocks) is t.Tensor and superblocks.is_cuda:
@@ -107,6 +108,36 @@ def _batched_gemm_device(t, a, sb, K: int, M: int, out, dev_err):
     return out
 
 
+class _HostStaging:
+    """Per-(device, stream) device staging of the overlapped host calls. It only grows,
+    and first waits for the calls still using it (they run on library streams, which
+    torch's allocator does not track)."""
+
+    def __init__(self):
+        import threading
+        self._bufs = {}
+        self._lock = threading.Lock()
+
+    def get(self, device_index: int, stream: int, nbytes: int):
+        key = (device_index, stream)
+        buf = self._bufs.get(key)  # the common case: an existing buffer large enough
+        if buf is not None and buf.numel() >= nbytes:
+            return buf
+        t = _lib.torch()
+        with self._lock:
+            buf = self._bufs.get(key)
+            if buf is None or buf.numel() < nbytes:
+                if buf is not None:
+                    check(lib().mb_int4_gemm_host_wait(stream), "mb_int4_gemm_host_wait")
+                buf = t.empty(max(nbytes, 4 << 20), dtype=t.uint8, device=t.device("cuda", device_index))
+                self._bufs[key] = buf
+            return buf
+
+
+_host_staging = _HostStaging()
+_HOST_SLOTS = 4  # MB_HOST_SLOTS
+
+
 def _batched_gemm_host(t, a, sb, K: int, M: int, out, dev_err, sync: bool):
     if a.dim() == 1:
         a = a.reshape(1, -1)
@@ -119,18 +150,25 @@ def _batched_gemm_host(t, a, sb, K: int, M: int, out, dev_err, sync: bool):
         raise ValueError(f"K*M = {K * M} is not a multiple of 256")
     if sb.dtype != t.uint8 or sb.numel() != K * M // 256 * 144:
         raise ValueError(f"superblock stream must be uint8 with {K * M // 256 * 144} bytes")
-    dev = sb.device
+    dev = sb.get_device()
     st = stream_of(dev)
-    # device staging for the activations and the output, reused by the calls of this stream
-    nin, nout = N * K * 2, N * M * 2
-    buf = _staging.get(dev, st, ((nin + 255) // 256) * 256 + nout)
-    base = buf.data_ptr()
-    check(lib().mb_int4_gemm_host(a.data_ptr(), sb.data_ptr(), out.data_ptr(), N, K, M, base,
-                                  base + ((nin + 255) // 256) * 256,
-                                  ptr(dev_err) if dev_err is not None else None, st), "mb_int4_gemm_host")
+    slot = ((N * K * 2 + 255) // 256 + (N * M * 2 + 255) // 256) * 256
+    buf = _host_staging.get(dev, st, _HOST_SLOTS * slot)
+    L = lib()
+    check(L.mb_int4_gemm_host_overlap(a.data_ptr(), sb.data_ptr(), out.data_ptr(), N, K, M, buf.data_ptr(),
+                                      buf.numel(), ptr(dev_err) if dev_err is not None else None, st),
+          "mb_int4_gemm_host_overlap")
     if sync:
-        t.cuda.current_stream(dev).synchronize()
+        check(L.mb_int4_gemm_host_wait(st), "mb_int4_gemm_host_wait")
     return out
+
+
+def host_wait(device=None) -> None:
+    """Wait until every host-buffer ``batched_gemm(..., sync=False)`` call enqueued on
+    the current stream of ``device`` has written its output."""
+    t = _lib.torch()
+    dev = t.device("cuda", t.cuda.current_device()) if device is None else t.device(device)
+    check(lib().mb_int4_gemm_host_wait(stream_of(dev)), "mb_int4_gemm_host_wait")
 
 
 def gemm_bytes(N: int, K: int, M: int) -> int:
@@ -142,6 +180,6 @@ def gemm_flops(N: int, K: int, M: int) -> int:
     return 2 * N * K * M
 
 
-__all__ = ["batched_gemm", "plan", "gemm_bytes", "gemm_flops"]
+__all__ = ["batched_gemm", "host_wait", "plan", "gemm_bytes", "gemm_flops"]
 
 _ = np  # numpy inputs are accepted through to_device

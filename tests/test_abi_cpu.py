@@ -98,6 +98,16 @@ def test_host_side_argument_validation(L):
     assert L.mb_decode_attn_cache(fake, fake, fake, fake, 1, 1, 20, 10, 128, 1.0, fake, 32768, 16.0, fake,
                                   1 << 30, None) == -2  # L > Lmax
     assert L.mb_int4_gemm_host(fake, fake, fake, 8, 3, 5, fake, fake, None, None) == -2
+    # overlapped host calls: staging is MB_HOST_SLOTS (4) fixed-size slots
+    slot = (32 * 3072 * 2 + 255) // 256 * 256 + (32 * 8192 * 2 + 255) // 256 * 256
+    assert L.mb_int4_gemm_host_staging_bytes(32, 3072, 8192) == 4 * slot
+    assert L.mb_int4_gemm_host_staging_bytes(0, 3072, 8192) == 0
+    big = ctypes.c_void_p(0x100000)
+    assert L.mb_int4_gemm_host_overlap(fake, fake, fake, 32, 3072, 8192, None, 4 * slot, None, None) == -1
+    assert L.mb_int4_gemm_host_overlap(fake, fake, fake, 8, 3, 5, big, 4 * slot, None, None) == -2
+    assert L.mb_int4_gemm_host_overlap(fake, fake, fake, 32, 3072, 8192, ctypes.c_void_p(0x100010), 4 * slot,
+                                       None, None) == -5  # staging not 256-byte aligned
+    assert L.mb_int4_gemm_host_overlap(fake, fake, fake, 32, 3072, 8192, big, 4 * slot - 256, None, None) == -3
     assert L.mb_int4_dequant(None, fake, 1, None) == -1
     assert L.mb_decode_attn(None, fake, fake, fake, 1, 1, 16, 128, 1.0, fake, 32768, 16.0, fake, 1 << 30, None) == -1
     # bad shapes -> MB_ERR_ARGS (-2)
@@ -119,7 +129,7 @@ def test_tensor_parallel_and_sampling_entries_validate_on_the_host(L):
     fake = ctypes.c_void_p(0x10000)
     bufs = (ctypes.c_void_p * 2)(0x10000, 0x20000)
     # key words, then two parities x 8 ranks of row slots; every 8-byte word carries
-    # two bf16 payload values and the call's epoch
+    # two fp16 payload values and the call's epoch
     assert L.mb_peer_buffer_bytes(16, 2048) == 16384 + 2 * 8 * (16 * 2048 // 2) * 8
     assert L.mb_peer_buffer_bytes(0, 2048) == 0 and L.mb_peer_buffer_bytes(65, 2048) == 0
     assert L.mb_peer_buffer_bytes(16, 100) == 0

@@ -148,3 +148,29 @@ def test_host_buffer_path_matches_device_path(cuda, N):
     for i in range(3):
         np.testing.assert_array_equal(hy[i].numpy().view(np.uint16), refs[i].view(np.uint16))
     close(hy[2].numpy(), O.gemm(xs[2], O.unpack_superblock_weights(st).reshape(K, M)))
+
+
+def test_overlapped_host_calls_across_slots_shapes_and_growth(cuda):
+    """Host-buffer calls with sync=False: more calls than staging slots, mixed batch
+    sizes (N > 32 included) and weights, and one call large enough to grow the
+    staging (which first waits for the calls in flight); after host_wait every
+    output equals the device path's bits."""
+    import torch
+    from moat_b200.gemm import batched_gemm, host_wait
+    shapes = [(512, 1024), (2048, 8192)]
+    sbs = {s: torch.from_numpy(O.quantize_pack_matrix(O.make_weights(s[0], s[1], 7 + i))).cuda()
+           for i, s in enumerate(shapes)}
+    calls = [(shapes[0], n) for n in (1, 7, 32, 40, 3, 16, 1, 9)] + [(shapes[1], 200)] + \
+            [(shapes[0], n) for n in (2, 33, 5)]
+    xs, hys, refs = [], [], []
+    for i, ((K, M), n) in enumerate(calls):
+        x = O.make_activations(n, K, 100 + i)
+        refs.append(batched_gemm(torch.from_numpy(x).cuda(), sbs[(K, M)], K, M).cpu().numpy())
+        xs.append(torch.from_numpy(x).pin_memory())
+        hys.append(torch.empty((n, M), dtype=torch.float16).pin_memory())
+    torch.cuda.synchronize()
+    for i, ((K, M), n) in enumerate(calls):
+        batched_gemm(xs[i], sbs[(K, M)], K, M, out=hys[i], sync=False)
+    host_wait()
+    for i in range(len(calls)):
+        np.testing.assert_array_equal(hys[i].numpy().view(np.uint16), refs[i].view(np.uint16), err_msg=str(calls[i]))
