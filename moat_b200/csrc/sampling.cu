@@ -257,6 +257,15 @@ __device__ __forceinline__ uint32_t warp_first_false(uint32_t lo, uint32_t hi, P
   return lo;
 }
 
+// The same order-preserving code for the fast path, two fp16 columns per 32-bit word
+// (negative: ~h, else h | 0x8000; -0 and +0 get neighbouring codes, which order and
+// decode the same way; NaNs are detected separately).
+__device__ __forceinline__ uint32_t code16p(uint32_t h) { return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u); }
+__device__ __forceinline__ uint32_t code16x2(uint32_t w) {
+  const uint32_t m = ((w & 0x80008000u) >> 15) * 0xFFFFu;  // 0xFFFF in each negative half
+  return (w ^ m) | (0x80008000u & ~m);
+}
+
 template <bool VEC>
 __device__ __forceinline__ void buf_load8(const uint16_t* buf, int o, int n, uint32_t (&w)[8]) {
   if (VEC && o + 8 <= n) {
@@ -295,6 +304,7 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
   extern __shared__ __align__(16) uint16_t ptab[];  // [size] the exp table, then the column buffer
   __shared__ unsigned long long red[kSampBlock / 32];
   __shared__ unsigned long long xa[kSampMaxCluster], xb[kSampMaxCluster];  // pushed: max keys, sums
+  __shared__ unsigned long long xa2[kSampMaxCluster];  // pushed: argmax keys of an erring row (fast path)
   __shared__ unsigned long long xlist[kSampMaxCluster][kSampMaxK];  // pushed to the leader: sorted local top-k
   __shared__ uint32_t xlen[kSampMaxCluster];
   __shared__ uint32_t hist[256], hist2[256];  // high-bit, then low-bit histograms of this CTA's indices
@@ -331,26 +341,54 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
   const int nc = ce - cb;  // this CTA's columns
   uint16_t* buf = a.buf_smem ? ptab + ((a.size + 7) & ~7) : a.scratch + row + cb;
 
-  // A: first index of the largest raw logit (NaN largest), row-wide, on the codes
+  // A: first index of the largest raw logit (NaN largest), row-wide, on the codes. The
+  // common case (T > 0, fp16 rows on 16-byte boundaries) needs only the maximum value:
+  // two columns per packed max; the column is found later only if the row errs.
+  const bool fast = VEC && a.scale && !a.f32;
   uint32_t bcode = 0;
   int bcol = -1;
-  for (int o = tid * 8; o < nc; o += kSampLd * 8 * kSampBlock) {  // kSampLd groups' loads in flight
-    uint32_t k8[kSampLd][8];
+  if (fast) {
+    uint32_t vmx = 0, nanm = 0;
+    const uint16_t* xr = static_cast<const uint16_t*>(a.logits) + row + cb;
+    for (int o = tid * 8; o < nc; o += 8 * kSampBlock) {
+      if (o + 8 <= nc) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(xr + o));
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int g = 0; g < kSampLd; ++g) samp_codes8<VEC>(a, row, cb + o + g * 8 * kSampBlock, ce, k8[g]);
-#pragma unroll
-    for (int g = 0; g < kSampLd; ++g)
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int oo = o + g * 8 * kSampBlock + u;
-        if (oo < nc && (bcol < 0 || k8[g][u] > bcode)) {  // columns ascend: strict > keeps the first
-          bcode = k8[g][u];
-          bcol = cb + oo;
+        for (int i = 0; i < 4; ++i) {
+          vmx = __vmaxu2(vmx, code16x2(w[i]));
+          nanm |= __vcmpgtu2(w[i] & 0x7FFF7FFFu, 0x7C007C00u);
+        }
+      } else {
+        for (int u = 0; o + u < nc; ++u) {
+          const uint32_t h = __ldg(xr + o + u);
+          vmx = __vmaxu2(vmx, code16p(h));
+          nanm |= (h & 0x7FFFu) > 0x7C00u ? 1u : 0u;
         }
       }
+    }
+    bcode = nanm ? 0xFFFFu : max(vmx & 0xFFFFu, vmx >> 16);
+  } else {
+    for (int o = tid * 8; o < nc; o += kSampLd * 8 * kSampBlock) {  // kSampLd groups' loads in flight
+      uint32_t k8[kSampLd][8];
+#pragma unroll
+      for (int g = 0; g < kSampLd; ++g) samp_codes8<VEC>(a, row, cb + o + g * 8 * kSampBlock, ce, k8[g]);
+#pragma unroll
+      for (int g = 0; g < kSampLd; ++g)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int oo = o + g * 8 * kSampBlock + u;
+          if (oo < nc && (bcol < 0 || k8[g][u] > bcode)) {  // columns ascend: strict > keeps the first
+            bcode = k8[g][u];
+            bcol = cb + oo;
+          }
+        }
+    }
   }
   unsigned long long best =
-      bcol < 0 ? 0ull : (static_cast<unsigned long long>(bcode) << 32) | (0xFFFFFFFFull - static_cast<uint32_t>(bcol));
+      fast ? static_cast<unsigned long long>(bcode) << 32
+           : (bcol < 0 ? 0ull
+                       : (static_cast<unsigned long long>(bcode) << 32) | (0xFFFFFFFFull - static_cast<uint32_t>(bcol)));
   best = block_max_u64_w0(best, red);  // its barriers also publish the staged table
   cluster_wait();                   // phase 0: every CTA of the cluster runs
   if (tid < C) st_cluster_u64(&xa[r], tid, best);
@@ -366,12 +404,42 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
   }
   __syncthreads();
   best = bcast;
-  const int amax = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
+  int amax = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull));
   const uint32_t acode = static_cast<uint32_t>(best >> 32);
-  const float m = samp_scaled(a, samp_raw(a, row + amax));
+  const float m = fast ? samp_scaled(a, decode16(acode)) : samp_scaled(a, samp_raw(a, row + amax));
   const uint32_t counter = *reinterpret_cast<volatile uint32_t*>(a.rng_state);
   const bool leader = r == 0;
   if (!isfinite(m)) {  // the reference raises on a non-finite maximum
+    if (fast) {  // the erring row's token is the first column of its maximum: one more join
+      uint32_t bc = 0;
+      int bj = -1;
+      for (int o = tid * 8; o < nc; o += 8 * kSampBlock) {
+        uint32_t k8[8];
+        samp_codes8<VEC>(a, row, cb + o, ce, k8);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (o + u < nc && (bj < 0 || k8[u] > bc)) {
+            bc = k8[u];
+            bj = cb + o + u;
+          }
+      }
+      unsigned long long key =
+          bj < 0 ? 0ull : (static_cast<unsigned long long>(bc) << 32) | (0xFFFFFFFFull - static_cast<uint32_t>(bj));
+      key = block_max_u64_w0(key, red);
+      if (tid < C) st_cluster_u64(&xa2[r], tid, key);
+      cluster_sync();
+      if (tid < 32) {
+        unsigned long long v = lane < C ? xa2[lane] : 0ull;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          const unsigned long long x = __shfl_xor_sync(0xffffffffu, v, o);
+          v = x > v ? x : v;
+        }
+        if (tid == 0) bcast = v;
+      }
+      __syncthreads();
+      amax = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(bcast & 0xFFFFFFFFull));
+    }
     if (leader && tid == 0) {
       if (a.err) atomicOr(a.err, MB_DEVERR_NONFINITE);
       a.tokens[n] = amax;
@@ -406,29 +474,70 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
     // probabilities, come first).
     unsigned long long acc = 0;
     uint32_t nclip = 0;
-    for (int o = tid * 8; o < nc; o += 8 * kSampBlock) {
-      uint32_t k8[8], jw[8];
-      samp_codes8<VEC>(a, row, cb + o, ce, k8);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        int j = jclip;
-        if (o + u < nc) {
-          if (lw > 0 && k8[u] >= lut_lo) {
-            j = cj[acode - k8[u]];
-          } else if (!below_clip) {
-            const float x = a.f32 ? decode32(k8[u]) : decode16(k8[u]);
-            j = samp_lut_index(samp_scaled(a, x) - m, a.step, a.size);
-          }
-          if (j == jclip) {
-            ++nclip;
-          } else {
-            acc += static_cast<uint32_t>(__half2float(__ushort_as_half(ptab[a.size - 1 - j])) * 16777216.0f);
-            if (a.scale) atomicAdd(&hist[255 - (j >> 7)], 1u);
-          }
-        }
-        jw[u] = static_cast<uint32_t>(j);
+    // one column whose index is not settled by the group test: look it up or compute it
+    auto settle = [&](int o, uint32_t c) {
+      int j;
+      if (below_clip && c < lut_lo)
+        j = jclip;
+      else if (lw > 0 && c >= lut_lo)
+        j = cj[acode - c];
+      else
+        j = samp_lut_index(samp_scaled(a, a.f32 ? decode32(c) : decode16(c)) - m, a.step, a.size);
+      if (a.scale) buf[o] = static_cast<uint16_t>(j);
+      if (j == jclip) {
+        ++nclip;
+      } else {
+        acc += static_cast<uint32_t>(__half2float(__ushort_as_half(ptab[a.size - 1 - j])) * 16777216.0f);
+        if (a.scale) atomicAdd(&hist[255 - (j >> 7)], 1u);
       }
-      if (a.scale) buf_store8<VEC>(buf, o, nc, jw);
+    };
+    if (fast) {
+      // two columns per packed compare against the table's lowest code; a group whose
+      // columns all clip costs one vector store, the others go through `settle` one
+      // set bit at a time (a warp pays for its busiest lane, not for every column)
+      const uint16_t* xr = static_cast<const uint16_t*>(a.logits) + row + cb;
+      const uint32_t lo2 = lut_lo * 0x10001u;
+      const uint32_t jj2 = static_cast<uint32_t>(jclip) * 0x10001u;
+      for (int o = tid * 8; o < nc; o += 8 * kSampBlock) {
+        uint32_t w[4] = {0u, 0u, 0u, 0u}, open;
+        if (o + 8 <= nc) {
+          const uint4 q = __ldg(reinterpret_cast<const uint4*>(xr + o));
+          w[0] = q.x;
+          w[1] = q.y;
+          w[2] = q.z;
+          w[3] = q.w;
+          open = 0xFFu;
+          if (below_clip) {
+            open = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t lt = __vcmpltu2(code16x2(w[i]), lo2);  // 0xFFFF where the column clips
+              open |= ((~lt & 1u) | ((~lt >> 15) & 2u)) << (2 * i);
+            }
+          }
+          nclip += 8u - __popc(open);
+          *reinterpret_cast<uint4*>(buf + o) = make_uint4(jj2, jj2, jj2, jj2);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)  // constant indices once unrolled: w stays in registers
+            if (o + u < nc) w[u >> 1] |= static_cast<uint32_t>(__ldg(xr + o + u)) << (16 * (u & 1));
+          open = (1u << (nc - o)) - 1u;
+        }
+        while (open) {
+          const int u = __ffs(open) - 1;
+          open &= open - 1u;
+          const uint32_t word = u < 2 ? w[0] : (u < 4 ? w[1] : (u < 6 ? w[2] : w[3]));
+          settle(o + u, code16p((u & 1) ? (word >> 16) : (word & 0xFFFFu)));
+        }
+      }
+    } else {
+      for (int o = tid * 8; o < nc; o += 8 * kSampBlock) {
+        uint32_t k8[8];
+        samp_codes8<VEC>(a, row, cb + o, ce, k8);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (o + u < nc) settle(o + u, k8[u]);
+      }
     }
     acc += static_cast<unsigned long long>(nclip) *
            static_cast<uint32_t>(__half2float(__ushort_as_half(ptab[0])) * 16777216.0f);

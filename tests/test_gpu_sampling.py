@@ -145,6 +145,32 @@ def test_non_finite_rows(cuda):
         sample_tokens(x, temperature=1e-5)
 
 
+def test_nan_rows_and_signed_zero_maxima(cuda):
+    """T > 0 on fp16 rows (the kernel's packed path): rows holding a NaN of either sign
+    err with the first NaN column as token (numpy.argmax's choice); rows whose maximum
+    is zero, held as -0 in some columns and +0 in others (or -0 alone), sample exactly
+    as the oracle does."""
+    x = S.make_logits(5, 1000, 21, 3.0, np.float16)
+    bits = x.view(np.uint16)
+    bits[0, 700] = 0xFE00      # negative quiet NaN
+    bits[0, 900] = 0x7E00
+    bits[1, 333] = 0x7C01      # positive signalling NaN
+    x[2] = -np.abs(x[2])
+    x[2, [10, 500]] = 0.0
+    bits[2, [20, 800]] = 0x8000  # -0
+    x[3] = -np.abs(x[3])
+    bits[3, [5, 6, 999]] = 0x8000
+    x[4] = -np.abs(x[4]) - 1.0
+    u = np.array([0.3, 0.3, 0.1, 0.7, 0.95], np.float32)
+    tok, lp, err = _run(x, 0.7, cuda, uniforms=u)
+    assert err & 4
+    assert tok[0] == 700 and tok[1] == 333
+    assert np.isnan(lp[0]) and np.isnan(lp[1])
+    otok, olp = S.sample_tokens(x[2:], 0.7, TABLE, 10.0, u[2:])
+    np.testing.assert_array_equal(tok[2:], otok)
+    np.testing.assert_allclose(lp[2:], olp, rtol=1e-6, atol=1e-6)
+
+
 def test_device_stream_counter_and_graph_replay(cuda):
     import torch
     from moat_b200.sampling import BatchSampler
