@@ -33,9 +33,12 @@
 //      2^-24);
 //   C..E  the probability p(j) = fp16(table[S-1-j] / sum) is a non-increasing function
 //      of j, and the row's top-k by (p descending, column ascending) lies in the union
-//      of the CTAs' own top-k: each CTA finds its k-th smallest index j_k (a high-bit
+//      of the CTAs' own top-k: each CTA finds its k-th smallest index j_k (T > 0 on
+//      aligned fp16 rows: pass B counted the unclipped columns per code-table offset,
+//      and j_k follows from a block prefix over the counts; otherwise a high-bit
 //      histogram, then one of the low 7 bits inside the chosen bin), the indices
-//      [j_lo, j_hi] whose probability equals p(j_k) (two warps, 32-way searches of p),
+//      [j_lo, j_hi] whose probability equals p(j_k) (two warps, 32-way searches of p,
+//      first over the 32 indices next to j_k),
 //      and takes every column below j_lo and the first ties in column order (a block
 //      prefix sum); it sorts these keys (p << 32 | ~column) and pushes them to the
 //      leader CTA, which ranks every key of the union by binary searches in the
@@ -308,6 +311,7 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
   __shared__ unsigned long long xlist[kSampMaxCluster][kSampMaxK];  // pushed to the leader: sorted local top-k
   __shared__ uint32_t xlen[kSampMaxCluster];
   __shared__ uint32_t hist[256], hist2[256];  // high-bit, then low-bit histograms of this CTA's indices
+  __shared__ uint32_t icnt[kSampLutMax];       // fast path: columns per code-table offset
   __shared__ uint32_t scan[kSampBlock / 32];
   __shared__ unsigned long long lc[kSampMaxK], sorted[kSampMaxK];
   __shared__ unsigned long long bcast;
@@ -329,6 +333,7 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
     hist[b] = 0;
     hist2[b] = 0;
   }
+  for (int b = threadIdx.x; b < kSampLutMax; b += kSampBlock) icnt[b] = 0;
   cluster_arrive_relaxed();  // phase 0: this CTA runs (awaited before the first remote store)
   pdl_wait();
   pdl_launch_dependents();
@@ -491,7 +496,53 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
         if (a.scale) atomicAdd(&hist[255 - (j >> 7)], 1u);
       }
     };
-    if (fast) {
+    // Fast path with a code table that reaches the clip index: an unclipped column's
+    // index is cj[i] of its table offset i = acode - code, a non-decreasing function of
+    // i, so pass B only counts the columns per offset (icnt) and leaves i (or 0xFFFF
+    // for a clipped column) in the column buffer; the sum, the k-th smallest index and
+    // every later classification read the counts and cj.
+    const bool fastb = fast && below_clip;
+    if (fastb) {
+      const uint16_t* xr = static_cast<const uint16_t*>(a.logits) + row + cb;
+      const uint32_t lo2 = lut_lo * 0x10001u;
+      for (int o = tid * 8; o < nc; o += 8 * kSampBlock) {
+        if (o + 8 <= nc) {
+          const uint4 q = __ldg(reinterpret_cast<const uint4*>(xr + o));
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+          uint32_t open = 0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t lt = __vcmpltu2(code16x2(w[i]), lo2);  // 0xFFFF where the column clips
+            open |= ((~lt & 1u) | ((~lt >> 15) & 2u)) << (2 * i);
+          }
+          nclip += 8u - __popc(open);
+          *reinterpret_cast<uint4*>(buf + o) = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
+          while (open) {
+            const int u = __ffs(open) - 1;
+            open &= open - 1u;
+            const uint32_t word = u < 2 ? w[0] : (u < 4 ? w[1] : (u < 6 ? w[2] : w[3]));
+            const uint32_t i = acode - code16p((u & 1) ? (word >> 16) : (word & 0xFFFFu));
+            atomicAdd(&icnt[i], 1u);
+            buf[o + u] = static_cast<uint16_t>(i);
+          }
+        } else {
+          for (int u = 0; o + u < nc; ++u) {
+            const uint32_t c = code16p(__ldg(xr + o + u));
+            if (c < lut_lo) {
+              buf[o + u] = 0xFFFFu;
+              ++nclip;
+            } else {
+              atomicAdd(&icnt[acode - c], 1u);
+              buf[o + u] = static_cast<uint16_t>(acode - c);
+            }
+          }
+        }
+      }
+      __syncthreads();
+      for (uint32_t i = tid; i < lw; i += kSampBlock)
+        acc += static_cast<unsigned long long>(icnt[i]) *
+               static_cast<uint32_t>(__half2float(__ushort_as_half(ptab[a.size - 1 - cj[i]])) * 16777216.0f);
+    } else if (fast) {
       // two columns per packed compare against the table's lowest code; a group whose
       // columns all clip costs one vector store, the others go through `settle` one
       // set bit at a time (a warp pays for its busiest lane, not for every column)
@@ -575,55 +626,106 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
       const uint32_t k = static_cast<uint32_t>(a.k);
       const uint32_t kl = min(k, static_cast<uint32_t>(nc));
       if (kl > 0) {  // CTA-uniform
-        // C, D: j_k from the high-bit histogram, then the low 7 bits inside its bin
-        if (tid < 32) {
-          uint32_t below = 0;
-          for (int i = lane; i < 256; i += 32) below += hist[i];
-#pragma unroll
-          for (int o = 16; o; o >>= 1) below += __shfl_xor_sync(0xffffffffu, below, o);
-          uint32_t above = 0;
-          const int b = below >= kl ? pick_bin_warp(hist, kl, &above) : -1;
-          if (tid == 0) {
-            sel[0] = static_cast<uint32_t>(b);
-            sel[1] = above;
-          }
-        }
-        __syncthreads();
         int jk = jclip;
-        if (static_cast<int>(sel[0]) >= 0) {
-          const int hb = 255 - static_cast<int>(sel[0]);
-          const uint32_t above_hi = sel[1];
-          for (int o = tid * 8; o < nc; o += 8 * kSampBlock) {
-            uint32_t jv[8];
-            buf_load8<VEC>(buf, o, nc, jv);
+        if (fastb) {
+          // C: the kl-th smallest offset from a block prefix over the counts (four
+          // offsets per thread); clip index if fewer than kl columns are unclipped
+          const int i0 = 4 * tid;
+          uint32_t c4 = 0;
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int j = static_cast<int>(jv[u]);
-              if (jv[u] != 0xFFFFu && j != jclip && (j >> 7) == hb) atomicAdd(&hist2[255 - (j & 127)], 1u);
+          for (int q = 0; q < 4; ++q) c4 += i0 + q < static_cast<int>(lw) ? icnt[i0 + q] : 0u;
+          uint32_t incl = c4;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += x;
+          }
+          if (lane == 31) scan[tid >> 5] = incl;
+          __syncthreads();
+          if (tid < 32) {
+            const uint32_t v = scan[tid];
+            uint32_t s2 = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const uint32_t x = __shfl_up_sync(0xffffffffu, s2, o);
+              if (lane >= o) s2 += x;
+            }
+            scan[tid] = s2 - v;
+            if (tid == 31) sel[0] = s2;  // unclipped columns of this CTA
+          }
+          __syncthreads();
+          const uint32_t excl = scan[tid >> 5] + incl - c4;
+          if (c4 > 0 && excl < kl && excl + c4 >= kl) {
+            uint32_t run = excl;
+            int istar = i0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              run += i0 + q < static_cast<int>(lw) ? icnt[i0 + q] : 0u;
+              if (run >= kl) {
+                istar = i0 + q;
+                break;
+              }
+            }
+            sel[2] = cj[istar];
+          }
+          __syncthreads();
+          if (sel[0] >= kl) jk = static_cast<int>(sel[2]);
+        } else {
+          // C, D: j_k from the high-bit histogram, then the low 7 bits inside its bin
+          if (tid < 32) {
+            uint32_t below = 0;
+            for (int i = lane; i < 256; i += 32) below += hist[i];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) below += __shfl_xor_sync(0xffffffffu, below, o);
+            uint32_t above = 0;
+            const int b = below >= kl ? pick_bin_warp(hist, kl, &above) : -1;
+            if (tid == 0) {
+              sel[0] = static_cast<uint32_t>(b);
+              sel[1] = above;
             }
           }
           __syncthreads();
-          if (tid < 32) {
-            uint32_t above;
-            const int lo = pick_bin_warp(hist2, kl - above_hi, &above);
-            if (tid == 0) sel[2] = static_cast<uint32_t>((hb << 7) | (255 - lo));
+          if (static_cast<int>(sel[0]) >= 0) {
+            const int hb = 255 - static_cast<int>(sel[0]);
+            const uint32_t above_hi = sel[1];
+            for (int o = tid * 8; o < nc; o += 8 * kSampBlock) {
+              uint32_t jv[8];
+              buf_load8<VEC>(buf, o, nc, jv);
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const int j = static_cast<int>(jv[u]);
+                if (jv[u] != 0xFFFFu && j != jclip && (j >> 7) == hb) atomicAdd(&hist2[255 - (j & 127)], 1u);
+              }
+            }
+            __syncthreads();
+            if (tid < 32) {
+              uint32_t above;
+              const int lo = pick_bin_warp(hist2, kl - above_hi, &above);
+              if (tid == 0) sel[2] = static_cast<uint32_t>((hb << 7) | (255 - lo));
+            }
+            __syncthreads();
+            jk = static_cast<int>(sel[2]);
           }
-          __syncthreads();
-          jk = static_cast<int>(sel[2]);
         }
         __syncthreads();  // every thread has read j_k before sel[] is reused
-        // [j_lo, j_hi]: two 32-way searches of the monotone p, one warp each
+        // [j_lo, j_hi]: 32-way searches of the monotone p, one warp each; the 32 indices
+        // next to j_k first (a run of equal probabilities rarely reaches past them),
+        // the whole range only if it does
         if (tid < 64) {
           const float pk = __half2float(__ushort_as_half(p16(jk)));
           if (tid < 32) {  // j_lo: first j in [0, j_k] with p(j) <= p(j_k)
-            const uint32_t f = warp_first_false(0u, static_cast<uint32_t>(jk), [&](uint32_t j) {
-              return __half2float(__ushort_as_half(p16(static_cast<int>(j)))) > pk;
-            });
+            auto above = [&](uint32_t j) { return __half2float(__ushort_as_half(p16(static_cast<int>(j)))) > pk; };
+            const uint32_t w0 = static_cast<uint32_t>(max(0, jk - 31));
+            const uint32_t f = (w0 == 0 || above(w0)) ? warp_first_false(w0, static_cast<uint32_t>(jk), above)
+                                                      : warp_first_false(0u, w0, above);
             if (tid == 0) sel[2] = f;
           } else {  // j_hi + 1: first j in [j_k, size] with p(j) < p(j_k) (size: past the table)
-            const uint32_t f = warp_first_false(static_cast<uint32_t>(jk), static_cast<uint32_t>(a.size), [&](uint32_t j) {
+            auto tie = [&](uint32_t j) {
               return static_cast<int>(j) < a.size && __half2float(__ushort_as_half(p16(static_cast<int>(j)))) >= pk;
-            });
+            };
+            const uint32_t w1 = static_cast<uint32_t>(min(a.size, jk + 31));
+            const uint32_t f = tie(w1) ? warp_first_false(w1, static_cast<uint32_t>(a.size), tie)
+                                       : warp_first_false(static_cast<uint32_t>(jk), w1, tie);
             if (tid == 32) {
               sel[3] = f - 1u;
               sel[1] = p16(jk);
@@ -632,6 +734,12 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
         }
         __syncthreads();
         const int jlo = static_cast<int>(sel[2]), jhi = static_cast<int>(sel[3]);
+        // a column-buffer entry's table index (fast path: a code-table offset or 0xFFFF)
+        auto jof = [&](uint32_t v) -> int {
+          if (!fastb) return static_cast<int>(v);
+          const int jt = cj[v < lw ? v : 0u];  // index always inside the table, sentinel or not
+          return v == 0xFFFFu ? jclip : jt;
+        };
         const uint32_t t = sel[1];  // fp16 bits of p(j_k)
         // E: contiguous column ranges of whole 8-column groups per thread, in column order
         const int sub = (((nc + kSampBlock - 1) / kSampBlock) + 7) & ~7;
@@ -643,7 +751,7 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             if (o + u >= o1) break;
-            const int j = static_cast<int>(jv[u]);
+            const int j = jof(jv[u]);
             if (j < jlo) {  // p(j) > p(j_k): fewer than kl such columns here
               const uint32_t slot = atomicAdd(&lcn, 1u);
               if (slot < kSampMaxK)
@@ -681,7 +789,7 @@ __global__ void __launch_bounds__(kSampBlock, 1) k_sample(SampArgs a) {
           buf_load8<VEC>(buf, o, o1, jv);
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            if (o + u < o1 && rank < need && static_cast<int>(jv[u]) >= jlo && static_cast<int>(jv[u]) <= jhi) {
+            if (o + u < o1 && rank < need && jof(jv[u]) >= jlo && jof(jv[u]) <= jhi) {
               lc[c_gt + rank] = (static_cast<unsigned long long>(t) << 32) | (0xFFFFFFFFull - (cb + o + u));
               ++rank;
             }
@@ -813,7 +921,7 @@ using namespace mb;
 // Per device, once: the kernel's shared-memory limit and how many clusters of each
 // size (1 CTA of 1024 threads per SM; sizes above 8 are non-portable) fit at once.
 constexpr int kSampMaxDevices = 64;
-constexpr size_t kSampSmemMax = 200 * 1024;  // dynamic: the table, column buffer and code table
+constexpr size_t kSampSmemMax = 184 * 1024;  // dynamic: the table, column buffer and code table
 struct SampDevice {
   bool ready = false;
   int capacity[kSampMaxCluster + 1] = {};
