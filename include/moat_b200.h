@@ -7,8 +7,9 @@
  *     host before anything was launched (the reference uses -1 for a null / unloaded
  *     context and -2 for invalid arguments, antigravity_c_api.h:129-130);
  *   - the caller owns every buffer (antigravity_c_api.h:76-83, 131-143); all pointers
- *     are DEVICE pointers except the host buffers of mb_int4_gemm_host; nothing here
- *     allocates device memory;
+ *     are DEVICE pointers except the host buffers of mb_int4_gemm_host and
+ *     mb_int4_gemm_host_overlap; nothing here allocates device memory (the overlapped
+ *     host calls create two copy streams and a few events per caller stream, once);
  *   - work is enqueued asynchronously on the caller's stream (`stream` is a
  *     cudaStream_t; NULL = legacy default stream). The reference is synchronous
  *     (waitUntilCompleted); callers that need the result on the host synchronise;
@@ -281,9 +282,10 @@ int32_t mb_argmax_keys_to_ids(const int64_t* keys, int32_t N, int32_t* ids, void
  * MB_DEVERR_TIMEOUT in dev_err; the outputs of that call are then undefined.
  * bufs[q] is rank q's exchange buffer as mapped in this process (bufs[rank] its own),
  * each of mb_peer_buffer_bytes(max_rows, D) bytes, zeroed before the first call.
- * state is a per-rank DEVICE array of 2 uint32 per exchange kind (zeroed once; the
- * epoch lives there, so a captured graph replays). Every rank must make the same
- * sequence of calls, each rank on its own GPU. */
+ * state is a per-rank DEVICE array of MB_PEER_STATE_WORDS uint32 per exchange kind
+ * (zeroed once; every row's epoch lives there, so a captured graph replays). Every
+ * rank must make the same sequence of calls, each rank on its own GPU. */
+#define MB_PEER_STATE_WORDS 64
 #define MB_IPC_HANDLE_BYTES 64
 
 /* Bytes of one exchange buffer for up to max_rows (<= 64) rows of D (multiple of 8)

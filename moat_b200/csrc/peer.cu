@@ -27,9 +27,9 @@
 //                   words, two fp16 per word
 // Epoch e (1, 2, ...) of a channel writes parity e & 1; a rank can only reach epoch
 // e + 2 after every rank has finished epoch e + 1, hence finished reading epoch e's
-// parity, so two parities never race. The epoch counter of each channel lives in a
-// small local state array (not shared) and is advanced by the last CTA of each call,
-// which keeps a captured CUDA graph replayable.
+// parity, so two parities never race. Each row's epoch lives in a small local state
+// array (one word per row and channel, not shared) and is stored by that row's CTA at
+// the end of each call, which keeps a captured CUDA graph replayable.
 //
 // Both kernels are chained with programmatic dependent launch: each waits for the
 // previous kernel to finish before it reads anything (griddepcontrol.wait), then lets
@@ -99,17 +99,12 @@ __device__ __forceinline__ uint32_t wait_ll(const uint2* p, uint32_t epoch, uint
   return v.x;
 }
 
-// The last CTA of a call advances the channel's epoch (read by the next call).
+// Every row keeps its own epoch word: both ranks make the same calls, so CTA n sees
+// the same epoch sequence everywhere, and the next call's CTA n reads the word only
+// after griddepcontrol.wait (this grid has completed and its writes are visible):
+// no fence, no arrival count.
 __device__ __forceinline__ void peer_finish(uint32_t* state, uint32_t epoch) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (atomicAdd(state + 1, 1u) == gridDim.x - 1) {
-      state[1] = 0;
-      state[0] = epoch;
-      __threadfence();
-    }
-  }
+  if (threadIdx.x == 0) state[blockIdx.x] = epoch;
 }
 
 __device__ __forceinline__ float block_sum_fixed(float v, float* part) {
@@ -123,7 +118,7 @@ __device__ __forceinline__ float block_sum_fixed(float v, float* part) {
   return tot;
 }
 
-// One CTA per row n. state = {epoch, arrivals} of channel 0.
+// One CTA per row n. state = the rows' epochs of channel 0.
 __global__ void __launch_bounds__(kPeerBlock) k_peer_add_rmsnorm(PeerSet ps, const uint16_t* __restrict__ partial,
                                                                  float* __restrict__ x, const float* __restrict__ w,
                                                                  int D, float eps, uint16_t* __restrict__ h,
@@ -133,9 +128,20 @@ __global__ void __launch_bounds__(kPeerBlock) k_peer_add_rmsnorm(PeerSet ps, con
   pdl_wait();               // the partial and the epoch state come from earlier kernels
   pdl_launch_dependents();  // the next kernel's prologue may overlap; it waits for this grid before reading x, h
   const int n = blockIdx.x;
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(state) + 1u;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(state + n) + 1u;
   const int par = epoch & 1u;
   const int chunks = D / 8;  // 16-byte chunks of a row: four words each
+  // this thread's residual and norm-weight values, loaded before the exchange so that
+  // their latency hides behind it (the element order of the sum below is unchanged)
+  constexpr int kPre = 16;  // D <= 4096 in registers; larger rows read the rest later
+  float* xr = x + static_cast<int64_t>(n) * D;
+  float xv[kPre], wv[kPre];
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    const int c = threadIdx.x + j * kPeerBlock;
+    xv[j] = c < D ? xr[c] : 0.0f;
+    wv[j] = c < D ? w[c] : 0.0f;
+  }
   auto slot = [&](uint8_t* buf, int src) {
     return reinterpret_cast<uint2*>(buf + kPeerRowOff) +
            ((static_cast<int64_t>(par) * kPeerMaxRanks + src) * ps.slot_elems + static_cast<int64_t>(n) * D) / 2;
@@ -174,21 +180,35 @@ __global__ void __launch_bounds__(kPeerBlock) k_peer_add_rmsnorm(PeerSet ps, con
   }
   __syncthreads();
   // 3. residual add and RMSNorm, element order as k_add_rmsnorm
-  float* xr = x + static_cast<int64_t>(n) * D;
   float ss = 0.0f;
-  for (int c = threadIdx.x; c < D; c += kPeerBlock) {
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    const int c = threadIdx.x + j * kPeerBlock;
+    if (c < D) {
+      const float v = xv[j] + delta[c];
+      xv[j] = v;
+      xr[c] = v;
+      ss = fmaf(v, v, ss);
+    }
+  }
+  for (int c = threadIdx.x + kPre * kPeerBlock; c < D; c += kPeerBlock) {
     const float v = xr[c] + delta[c];
     xr[c] = v;
     ss = fmaf(v, v, ss);
   }
   const float inv = rsqrtf(block_sum_fixed(ss, part) / static_cast<float>(D) + eps);
-  for (int c = threadIdx.x; c < D; c += kPeerBlock)
+#pragma unroll
+  for (int j = 0; j < kPre; ++j) {
+    const int c = threadIdx.x + j * kPeerBlock;
+    if (c < D) h[static_cast<int64_t>(n) * D + c] = __half_as_ushort(__float2half_rn(xv[j] * inv * wv[j]));
+  }
+  for (int c = threadIdx.x + kPre * kPeerBlock; c < D; c += kPeerBlock)
     h[static_cast<int64_t>(n) * D + c] = __half_as_ushort(__float2half_rn(xr[c] * inv * w[c]));
   peer_finish(state, epoch);
 }
 
 // One CTA per row n: key of this rank's best logit, exchanged, max over ranks -> ids[n].
-// state = {epoch, arrivals} of channel 1.
+// state = the rows' epochs of channel 1.
 constexpr int kPeerArgBlock = 1024;
 
 __global__ void __launch_bounds__(kPeerArgBlock) k_peer_argmax(PeerSet ps, const uint16_t* __restrict__ logits, int V,
@@ -198,7 +218,7 @@ __global__ void __launch_bounds__(kPeerArgBlock) k_peer_argmax(PeerSet ps, const
   pdl_wait();
   pdl_launch_dependents();
   const int n = blockIdx.x;
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(state) + 1u;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(state + n) + 1u;
   const int par = epoch & 1u;
   unsigned long long best =
       thread_best_key(logits + static_cast<int64_t>(n) * V, V, col0, threadIdx.x, kPeerArgBlock);

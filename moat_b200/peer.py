@@ -24,6 +24,7 @@ from ._lib import check, lib, stream_of
 
 HANDLE_BYTES = 64
 DEVERR_TIMEOUT = 1
+STATE_WORDS = 64  # MB_PEER_STATE_WORDS: one epoch word per row and exchange kind
 
 
 class PeerExchange:
@@ -79,8 +80,8 @@ class PeerExchange:
             self.close(barrier=False)
             raise RuntimeError("peer exchange could not map the other ranks' buffers: " + "; ".join(failures))
         self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
-        # {epoch, arrivals} per exchange kind: [0:2] add_rmsnorm, [2:4] argmax
-        self.state = t.zeros(4, dtype=t.int32, device=self.dev)
+        # every row's epoch per exchange kind (MB_PEER_STATE_WORDS each): add_rmsnorm, argmax
+        self.state = t.zeros(2 * STATE_WORDS, dtype=t.int32, device=self.dev)
         t.cuda.synchronize(self.dev)
         dist.barrier(group=group)  # every buffer is zeroed and mapped before anyone stores
 
@@ -98,9 +99,10 @@ class PeerExchange:
         """ids = the global greedy choice over every rank's column range of the logits."""
         N, V = logits.shape
         st = stream_of(self.dev) if stream is None else stream
+        state1 = self.state.data_ptr() + 4 * STATE_WORDS  # the argmax channel's row epochs
         check(lib().mb_peer_argmax(self._bufs, self.world, self.rank, self.slot_elems, self.timeout_ns,
-                                   logits.data_ptr(), N, V, int(col0), ids.data_ptr(), self.state.data_ptr() + 8,
-                                   err.data_ptr(), st), "mb_peer_argmax")
+                                   logits.data_ptr(), N, V, int(col0), ids.data_ptr(), state1, err.data_ptr(), st),
+              "mb_peer_argmax")
 
     def close(self, barrier: bool = True):
         """Unmap the peers' buffers and free this rank's (after every rank has finished

@@ -118,7 +118,7 @@ def test_peer_exchange_one_rank_equals_local_kernels(cuda):
     g = torch.Generator(device=cuda)
     g.manual_seed(4)
     bufs = _exchange_buffers(cuda, 1, N, D)
-    state = torch.zeros(4, dtype=torch.int32, device=cuda)
+    state = torch.zeros(128, dtype=torch.int32, device=cuda)  # 64 row epochs per exchange kind
     err = torch.zeros(1, dtype=torch.int32, device=cuda)
     x_a = torch.randn((N, D), generator=g, device=cuda)
     x_b = x_a.clone()
@@ -134,12 +134,13 @@ def test_peer_exchange_one_rank_equals_local_kernels(cuda):
         assert L.mb_add_rmsnorm(x_b.data_ptr(), y.data_ptr(), w.data_ptr(), N, D, 1e-6, h_b.data_ptr(), _st()) == 0
         logits = torch.randn((N, V), generator=g, device=cuda).half()
         assert L.mb_peer_argmax(_ptrs(bufs), 1, 0, N * D, 10**9, logits.data_ptr(), N, V, 0, ids_a.data_ptr(),
-                                state.data_ptr() + 8, err.data_ptr(), _st()) == 0
+                                state.data_ptr() + 256, err.data_ptr(), _st()) == 0
         assert L.mb_argmax_f16(logits.data_ptr(), N, V, ids_b.data_ptr(), _st()) == 0
         torch.cuda.synchronize()
         assert torch.equal(x_a, x_b) and torch.equal(h_a, h_b) and torch.equal(ids_a, ids_b)
     assert int(err.item()) == 0
-    assert state.cpu().tolist() == [5, 0, 5, 0]
+    epochs = state.cpu().tolist()
+    assert epochs[:N] == [5] * N and epochs[64:64 + N] == [5] * N and not any(epochs[N:64] + epochs[64 + N:])
 
 
 def test_peer_wait_gives_up_with_error_bit(cuda):
@@ -153,7 +154,7 @@ def test_peer_wait_gives_up_with_error_bit(cuda):
     L = lib()
     N, D = 2, 256
     bufs = _exchange_buffers(cuda, 2, N, D)
-    state = torch.zeros(4, dtype=torch.int32, device=cuda)
+    state = torch.zeros(128, dtype=torch.int32, device=cuda)
     err = torch.zeros(1, dtype=torch.int32, device=cuda)
     x = torch.zeros((N, D), device=cuda)
     w = torch.ones(D, device=cuda)
