@@ -97,6 +97,8 @@ def gather_heads(local, bounds: Sequence[Tuple[int, int]], group=None):
     dist.all_gather_into_tensor(recv, send, group=group)
     recv = recv.view(world, T, hmax, d)
     H = bounds[-1][1]
+    if all(h1 - h0 == hmax for h0, h1 in bounds):  # equal shards: one transposing copy
+        return recv.transpose(0, 1).reshape(T, H, d)
     out = torch.empty((T, H, d), dtype=local.dtype, device=local.device)
     for r, (h0, h1) in enumerate(bounds):
         out[:, h0:h1] = recv[r, :, :h1 - h0]
