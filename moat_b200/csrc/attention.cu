@@ -18,7 +18,8 @@
 //      initial contents (pass 1 resets the arrival counters).
 // Rows of up to 2048 keys (the decode step's caches) take one launch instead: one CTA
 // per row streams its K and then its V rows through a shared-memory ring with bulk
-// copies, holding the row's scores in shared memory (k_attn_stream).
+// copies, holding the row's scores in shared memory (k_attn_stream); with fewer rows
+// than SMs, a cluster of CTAs shares each row (k_attn_stream_split).
 #include <algorithm>
 
 #include "common.cuh"
@@ -657,6 +658,237 @@ __global__ void __launch_bounds__((kStrWarps + 1) * 32) k_attn_stream(const uint
   }
 }
 
+// Split form for few rows (fewer than the SMs, e.g. a tensor-parallel rank's heads):
+// one cluster of S CTAs per row, CTA c streaming the keys [c * per, (c + 1) * per) of
+// the row's valid length through its own ring exactly as k_attn_stream does, so a row
+// moves at S CTAs' rate. The row max, the LUT sum and the partial outputs are joined
+// through distributed shared memory: a CTA stores its value into a slot of every CTA
+// (the outputs only into the leader's) and arrives on that CTA's mbarrier (release,
+// cluster scope); a CTA reads the slots once its own mbarrier has seen all S arrivals
+// (acquire, bounded wait). The only cluster barrier is the one after the mbarriers are
+// initialised, which every thread passes before the producer warp splits off. Same
+// per-element arithmetic as k_attn_stream; the sums run over the S CTAs in order.
+constexpr int kAttnSplitMax = 8;  // portable cluster size
+
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  auto try_once = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_once()) return true;
+  const long long t0 = clock64();
+  while (!try_once())
+    if (clock64() - t0 > kWaitBudget) return false;
+  return true;
+}
+
+template <int TPR>
+__global__ void __launch_bounds__((kStrWarps + 1) * 32) k_attn_stream_split(
+    const uint16_t* __restrict__ q, const uint16_t* __restrict__ k, const uint16_t* __restrict__ v,
+    uint16_t* __restrict__ out, int Lg, int64_t kvs, int Lc, float scale, const uint16_t* __restrict__ table,
+    int size, float step, AttnWs w) {
+  constexpr int D = TPR * 8;
+  constexpr int KS = kStrStage / (D * 2);
+  constexpr int KW = 32 / TPR;
+  constexpr int IT = KS / (kStrWarps * KW);
+  constexpr int CT = kStrWarps * 32;
+  extern __shared__ __align__(128) uint8_t dyn[];
+  uint8_t* ring = dyn;                                               // [kStrRing][kStrStage]
+  float* sc = reinterpret_cast<float*>(dyn + kStrRing * kStrStage);  // [Lc]
+  float* red = sc + ((Lc + 3) & ~3);                                 // [kStrWarps][D]
+  float* xpart = red + kStrWarps * D;                                // [S][D]: the leader's slots
+  __shared__ __align__(8) uint64_t full[kStrRing], empty[kStrRing], xbar[3];
+  __shared__ float sh[kStrWarps];
+  __shared__ float xmax[kAttnSplitMax], xsum[kAttnSplitMax];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = static_cast<int>(gridDim.x);  // cluster dims (S, 1, 1)
+  const int c = static_cast<int>(cluster_ctarank());
+  const int row = blockIdx.y;
+  if (threadIdx.x == 0) {
+    for (int r = 0; r < kStrRing; ++r) {
+      mbar_init(full + r, 1);
+      mbar_init(empty + r, kStrWarps);
+    }
+    for (int i = 0; i < 3; ++i) mbar_init(xbar + i, S);  // one arrival per CTA of the cluster
+    fence_mbar_init();
+  }
+  cluster_sync();  // every CTA's mbarriers exist before anyone arrives on them remotely
+  pdl_wait();      // q, K, V and the lengths may come from the previous kernel
+  pdl_launch_dependents();
+  const int L = attn_len(w, row, Lg);
+  const int per = ((L + S - 1) / S + 15) & ~15;  // <= Lc: the host sized Lc for Lg >= L
+  const int l0 = min(L, c * per);
+  const int n = min(L, l0 + per) - l0;  // this CTA's keys
+  const int nK = (n + KS - 1) / KS;
+  if (warp == kStrWarps) {
+    // ---------------- producer: this CTA's K rows, then its V rows ----------------
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      const uint8_t* kb = reinterpret_cast<const uint8_t*>(k + static_cast<int64_t>(row) * kvs + static_cast<int64_t>(l0) * D);
+      const uint8_t* vb = reinterpret_cast<const uint8_t*>(v + static_cast<int64_t>(row) * kvs + static_cast<int64_t>(l0) * D);
+      for (int s = 0; s < 2 * nK; ++s) {
+        const int slot = s % kStrRing;
+        if (s >= kStrRing && !mbar_wait(empty + slot, ((s / kStrRing) - 1) & 1) && w.err)
+          atomicOr(w.err, MB_DEVERR_TIMEOUT);
+        const int kk = s < nK ? s : s - nK;
+        const uint32_t bytes = static_cast<uint32_t>(min(KS, n - kk * KS)) * D * 2;
+        mbar_expect_tx(full + slot, bytes);
+        bulk_load_g2s(ring + slot * kStrStage, (s < nK ? kb : vb) + static_cast<size_t>(kk) * KS * D * 2, bytes,
+                      full + slot, pol);
+      }
+    }
+    return;
+  }
+  // ---------------- consumers ----------------
+  const int sub = lane % TPR, ks = lane / TPR;
+  float qf[8];
+  {
+    const uint4 qv = *reinterpret_cast<const uint4*>(q + static_cast<int64_t>(row) * D + sub * 8);
+    const __half2* h = reinterpret_cast<const __half2*>(&qv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      qf[2 * i] = f.x;
+      qf[2 * i + 1] = f.y;
+    }
+  }
+  float m = -INFINITY;
+  for (int s = 0; s < nK; ++s) {
+    const int slot = s % kStrRing;
+    if (!mbar_wait(full + slot, (s / kStrRing) & 1) && lane == 0 && w.err) atomicOr(w.err, MB_DEVERR_TIMEOUT);
+    const int j0 = s * KS, rows = min(KS, n - j0);
+    const uint8_t* st = ring + slot * kStrStage;
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      const int kr = (it * kStrWarps + warp) * KW + ks;
+      float dot = 0.0f;
+      if (kr < rows) {
+        const uint4 kv = ld_shared_v4u(st + kr * D * 2 + sub * 16);
+        const __half2* h = reinterpret_cast<const __half2*>(&kv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h[i]);
+          dot = fmaf(qf[2 * i], f.x, dot);
+          dot = fmaf(qf[2 * i + 1], f.y, dot);
+        }
+      }
+#pragma unroll
+      for (int o = TPR / 2; o >= 1; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      if (sub == 0 && kr < rows) {
+        const float x = dot * scale;
+        sc[j0 + kr] = x;
+        m = nanmax_f(m, x);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + slot);
+  }
+  m = cons_reduce(m, sh, true);
+  // row max: this CTA's max into slot c of every CTA, then wait for all S
+  if (threadIdx.x < S) {
+    st_shared_cluster_f32(mapa_shared(smem_u32(&xmax[c]), threadIdx.x), m);
+    mbar_arrive_remote(mapa_shared(smem_u32(&xbar[0]), threadIdx.x));
+  }
+  if (!mbar_wait_cluster(&xbar[0], 0) && threadIdx.x == 0 && w.err) atomicOr(w.err, MB_DEVERR_TIMEOUT);
+  float gm = -INFINITY;
+  for (int i = 0; i < S; ++i) gm = nanmax_f(gm, xmax[i]);
+  float acc = 0.0f;
+  for (int j = threadIdx.x; j < n; j += CT) {
+    const float e = lut_exp(table, sc[j] - gm, step, size);
+    sc[j] = e;
+    acc += e;
+  }
+  acc = cons_reduce(acc, sh, false);
+  if (threadIdx.x < S) {
+    st_shared_cluster_f32(mapa_shared(smem_u32(&xsum[c]), threadIdx.x), acc);
+    mbar_arrive_remote(mapa_shared(smem_u32(&xbar[1]), threadIdx.x));
+  }
+  if (!mbar_wait_cluster(&xbar[1], 0) && threadIdx.x == 0 && w.err) atomicOr(w.err, MB_DEVERR_TIMEOUT);
+  float tot = 0.0f;
+  for (int i = 0; i < S; ++i) tot += xsum[i];
+  const float sum = tot > 0.0f ? tot : 1.0f;
+  for (int j = threadIdx.x; j < n; j += CT) sc[j] = __half2float(__float2half_rn(__fdiv_rn(sc[j], sum)));
+  named_bar_sync(1, CT);
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+  for (int s = nK; s < 2 * nK; ++s) {
+    const int slot = s % kStrRing;
+    if (!mbar_wait(full + slot, (s / kStrRing) & 1) && lane == 0 && w.err) atomicOr(w.err, MB_DEVERR_TIMEOUT);
+    const int j0 = (s - nK) * KS, rows = min(KS, n - j0);
+    const uint8_t* st = ring + slot * kStrStage;
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      const int kr = (it * kStrWarps + warp) * KW + ks;
+      if (kr < rows) {
+        const float p = sc[j0 + kr];
+        const uint4 vv = ld_shared_v4u(st + kr * D * 2 + sub * 16);
+        const __half2* h = reinterpret_cast<const __half2*>(&vv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(h[i]);
+          o[2 * i] = fmaf(p, f.x, o[2 * i]);
+          o[2 * i + 1] = fmaf(p, f.y, o[2 * i + 1]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + slot);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int x = TPR; x < 32; x <<= 1) o[i] += __shfl_xor_sync(0xffffffffu, o[i], x);
+  if (ks == 0)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[warp * D + sub * 8 + i] = o[i];
+  named_bar_sync(1, CT);
+  // this CTA's partial output into the leader's slot c, then one arrival there (the
+  // barrier above orders every thread's stores before thread 0's release)
+  for (int dd = threadIdx.x; dd < D; dd += CT) {
+    float t = 0.0f;
+    for (int g = 0; g < kStrWarps; ++g) t += red[g * D + dd];
+    st_shared_cluster_f32(mapa_shared(smem_u32(&xpart[c * D + dd]), 0), t);
+  }
+  if (threadIdx.x < D) asm volatile("fence.acq_rel.cluster;" ::: "memory");  // visible cluster-wide
+  named_bar_sync(1, CT);
+  if (threadIdx.x == 0) mbar_arrive_remote(mapa_shared(smem_u32(&xbar[2]), 0));
+  if (c == 0) {
+    if (!mbar_wait_cluster(&xbar[2], 0) && threadIdx.x == 0 && w.err) atomicOr(w.err, MB_DEVERR_TIMEOUT);
+    for (int dd = threadIdx.x; dd < D; dd += CT) {
+      float t = 0.0f;
+      for (int i = 0; i < S; ++i) t += xpart[i * D + dd];
+      out[static_cast<int64_t>(row) * D + dd] = __half_as_ushort(__float2half_rn(t));
+    }
+  }
+}
+
+// Split size for `rows` rows of up to Lg keys: about two CTAs per SM in all, at most
+// kAttnSplitMax, at least 16 keys each; 1 = the one-CTA-per-row kernel.
+static int attn_split(int rows, int Lg) {
+  if (rows >= 148) return 1;
+  return std::max(1, std::min({kAttnSplitMax, (2 * 148) / rows, (Lg + 15) / 16}));
+}
+
+static size_t attn_split_smem(int Lg, int d, int S) {
+  const int Lc = ((Lg + S - 1) / S + 15) & ~15;
+  return static_cast<size_t>(kStrRing) * kStrStage + static_cast<size_t>((Lc + 3) & ~3) * 4 +
+         static_cast<size_t>(kStrWarps) * d * 4 + static_cast<size_t>(S) * d * 4;
+}
+
 static size_t attn_stream_smem(int Lg, int d) {
   return static_cast<size_t>(kStrRing) * kStrStage + static_cast<size_t>((Lg + 3) & ~3) * 4 +
          static_cast<size_t>(kStrWarps) * d * 4;
@@ -725,6 +957,34 @@ static int32_t attn_launch(const uint16_t* q, const uint16_t* k, const uint16_t*
                            cudaStream_t st) {
   if (L <= kAttnFusedMax) {
     const bool aligned = ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) == 0;
+    const int S = attn_split(rows, L);
+    if (aligned && L <= kAttnStreamMax && S > 1 && rows <= 65535) {  // few rows: S CTAs per row
+      const size_t smem = attn_split_smem(L, TPR * 8, S);
+      if (cudaFuncSetAttribute(k_attn_stream_split<TPR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem)) != cudaSuccess)
+        return MB_ERR_LAUNCH;
+      const int Lc = ((L + S - 1) / S + 15) & ~15;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(S, rows);
+      cfg.blockDim = dim3((kStrWarps + 1) * 32);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[2];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = S;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 2;
+      if (cudaLaunchKernelEx(&cfg, k_attn_stream_split<TPR>, q, k, v, out, L, kvs, Lc, scale, table, size, step, w) !=
+          cudaSuccess) {
+        (void)cudaGetLastError();
+        return MB_ERR_LAUNCH;
+      }
+      return MB_OK;
+    }
     if (aligned && L <= kAttnStreamMax) {  // kvs * 2 bytes is a multiple of 16 for every d >= 8
       const size_t smem = attn_stream_smem(L, TPR * 8);
       if (cudaFuncSetAttribute(k_attn_stream<TPR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
