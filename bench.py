@@ -675,7 +675,8 @@ def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 256, prompt: in
             "metric": "decode tok/s", "tok_per_s": N / ms * 1e3, "ms_per_step": ms, "steps": steps,
             "prompt": prompt, "prefill_s": prefill_s, "prefill_tok_per_s": N * prompt / prefill_s, "graph": True,
             "tensor_parallel": world, "scaling": "strong" if world > 1 else None,
-            "exchange": "NVLink peer stores (mb_peer_add_rmsnorm, mb_peer_argmax)" if world > 1 else None,
+            "exchange": ("NVLink peer stores from the o_proj / down GEMM epilogues (mb_int4_gemm_peer, "
+                         "mb_peer_sum_rmsnorm) and mb_peer_argmax") if world > 1 else None,
             "bytes_per_step": step_bytes, "GBps": step_bytes / ms / 1e6, "device_error_bits": err,
             "replicas": replicas, "tp_check": tp_check, "cpu_baseline": cpu,
             "data": "synthetic (random-init weights quantized to INT4; seeded random prompt ids)"}
@@ -768,9 +769,13 @@ def exchange_side(dev, rank: int, world: int, rows: int = 16, hidden: int = 2048
     exchange`` under torchrun): ``add_rmsnorm`` of [N, D] fp16 partials over NVLink peer
     stores, the greedy ``argmax`` over [N, V/G] logits per rank, and an NCCL
     ``all_reduce`` of the same [N, D] fp16 rows for comparison; CUDA events over
-    back-to-back calls after warm-up, the maximum over ranks. ``*_us``: the calls
-    replayed from one CUDA graph, as in the decode step; ``*_eager_us``: launched one by
-    one from Python (host-bound)."""
+    back-to-back calls after warm-up, the maximum over ranks. Also a row-parallel
+    o_proj (``[N, D / world] x [D / world, D]``) with its join: ``o_proj_gemm_join``
+    (the GEMM's partial through HBM, the join kernel stores it to the peers) against
+    ``o_proj_gemm_join_fused`` (the GEMM's epilogue stores its rows into the exchange
+    buffers, ``mb_int4_gemm_peer``). ``*_us``: the calls replayed from one CUDA graph,
+    as in the decode step; ``*_eager_us``: launched one by one from Python
+    (host-bound)."""
     import torch
     import torch.distributed as dist
     from moat_b200.peer import PeerExchange
@@ -817,9 +822,30 @@ def exchange_side(dev, rank: int, world: int, rows: int = 16, hidden: int = 2048
         dist.all_reduce(m, op=dist.ReduceOp.MAX)
         return float(m.item())
 
+    # a row-parallel o_proj (K = D / world rows of this rank) and its join: the GEMM's
+    # partial through HBM into the join kernel, or stored by the GEMM's epilogue
+    from moat_b200._lib import lib
+    from moat_b200.dequant import quantize_to_superblocks
+    Ko = D // world
+    wo = quantize_to_superblocks((0.02 * torch.randn((Ko, D), generator=g, device=dev)).reshape(-1))
+    act = torch.randn((N, Ko), generator=g, device=dev).half()
+    o = torch.empty((N, D), dtype=torch.float16, device=dev)
+
+    def gemm_join():
+        st = torch.cuda.current_stream(dev).cuda_stream
+        lib().mb_int4_gemm(act.data_ptr(), wo.data_ptr(), o.data_ptr(), N, Ko, D, err.data_ptr(), st)
+        px.add_rmsnorm(o, x, w, 1e-6, h, err, st)
+
+    def gemm_join_fused():
+        st = torch.cuda.current_stream(dev).cuda_stream
+        px.gemm(act, wo, Ko, D, err, st)
+        px.sum_rmsnorm(x, w, 1e-6, h, err, st)
+
     calls = {"add_rmsnorm": lambda: px.add_rmsnorm(partial, x, w, 1e-6, h, err),
              "argmax": lambda: px.argmax(logits, rank * Vl, ids, err),
-             "nccl_all_reduce": lambda: dist.all_reduce(red)}
+             "nccl_all_reduce": lambda: dist.all_reduce(red),
+             "o_proj_gemm_join": gemm_join,
+             "o_proj_gemm_join_fused": gemm_join_fused}
     try:
         out = {"world": world, "rows": N, "hidden": D, "vocab_per_rank": Vl, "iters": iters}
         for name, fn in calls.items():

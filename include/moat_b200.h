@@ -308,6 +308,27 @@ int32_t mb_peer_add_rmsnorm(void* const* bufs, int32_t world, int32_t rank, int6
                             const uint16_t* partial, float* x, const float* w, int32_t N, int32_t D, float eps,
                             uint16_t* h, uint32_t* state, uint32_t* dev_err, void* stream);
 
+/* Row-parallel projection fused with its join: the GEMM of mb_int4_gemm (this rank's
+ * partial [N, M] of a row-split projection, o_proj or down of the reference's
+ * transformer.py:148-158 on one device), whose epilogue stores its fp16 rows straight
+ * into every rank's exchange buffer as the words mb_peer_add_rmsnorm would store (the
+ * same fp16 rounding as mb_int4_gemm's output), so the partial never goes to HBM and
+ * the join that follows, mb_peer_sum_rmsnorm with the same state, only waits for the
+ * other ranks' rows, sums and normalises. state is read (this call's epoch is
+ * state[n] + 1), not advanced: the join advances it. M is the join's D; N <= 64,
+ * N * M <= slot_elems. Shapes off the fast GEMM plan (K % 8 != 0, M % 128 != 0,
+ * act or sb not 16-byte aligned) return MB_ERR_UNSUPPORTED before any launch: use
+ * mb_int4_gemm + mb_peer_add_rmsnorm for those. */
+int32_t mb_int4_gemm_peer(const uint16_t* act, const uint8_t* sb, int32_t N, int32_t K, int32_t M,
+                          void* const* bufs, int32_t world, int32_t rank, int64_t slot_elems, const uint32_t* state,
+                          uint32_t* dev_err, void* stream);
+
+/* The join after mb_int4_gemm_peer: mb_peer_add_rmsnorm whose partial rows every rank
+ * has already stored through its mb_int4_gemm_peer call of this epoch. */
+int32_t mb_peer_sum_rmsnorm(void* const* bufs, int32_t world, int32_t rank, int64_t slot_elems, int64_t timeout_ns,
+                            float* x, const float* w, int32_t N, int32_t D, float eps, uint16_t* h, uint32_t* state,
+                            uint32_t* dev_err, void* stream);
+
 /* Greedy choice over a column-split vocabulary: this rank holds logits [N, V] of
  * columns [col0, col0 + V); ids[n] = the global first index of the largest logit over
  * all ranks (NaN largest, -0 == +0), as mb_argmax_f16 over the whole row. */

@@ -60,6 +60,9 @@ SIGNATURES = {
                                      _vp, _vp, _vp]),
     "mb_peer_argmax": (_c_i32, [_vp, _c_i32, _c_i32, _c_i64, _c_i64, _vp, _c_i32, _c_i32, _c_i32, _vp, _vp, _vp,
                                 _vp]),
+    "mb_int4_gemm_peer": (_c_i32, [_vp, _vp, _c_i32, _c_i32, _c_i32, _vp, _c_i32, _c_i32, _c_i64, _vp, _vp, _vp]),
+    "mb_peer_sum_rmsnorm": (_c_i32, [_vp, _c_i32, _c_i32, _c_i64, _c_i64, _vp, _vp, _c_i32, _c_i32, _c_f, _vp, _vp,
+                                     _vp, _vp]),
     "mb_sample_workspace_size": (_c_sz, [_c_i32, _c_i32]),
     "mb_sample_tokens": (_c_i32, [_vp, _c_i32, _c_i32, _c_i32, _c_f, _c_i32, _vp, _c_i32, _c_f, _vp, ctypes.c_uint64,
                                   _vp, _vp, _vp, _vp, _c_sz, _vp, _vp]),

@@ -35,6 +35,7 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "peer_ll.cuh"
 
 namespace mb {
 
@@ -104,6 +105,13 @@ struct GemmParams {
   int owner[8];              // the CTA that owns strip group g
   int split;                 // 1: the kKG warps of a group take alternate stages (all 8 slices each);
                              // 0: they take alternate slices of every stage
+  // Row-parallel exchange (XCH kernels only): instead of writing out, the owners store
+  // their fp16 rows as low-latency words into slot [epoch parity][xrank] of every
+  // rank's exchange buffer (layout in peer_ll.cuh; M is the join's row width D).
+  uint8_t* xbuf[kPeerMaxRanks];
+  const uint32_t* xstate;  // the join channel's row epochs: this call's epoch is state[row] + 1
+  long long xslot;         // fp16 elements of one exchange slot
+  int xworld, xrank, xrow0;  // xrow0: exchange row of this launch's first batch row
 };
 
 // Activations in shared memory: chunks of 128 k values (one stage) by N rows; a row
@@ -256,9 +264,10 @@ __device__ __forceinline__ void consume_slice(const NibConst& kc, uint32_t r0, u
   }
 }
 
-// NT: n-tiles of 8 batch rows (1, 2, 4); WS: strip width; P: row phases (1, 2).
+// NT: n-tiles of 8 batch rows (1, 2, 4); WS: strip width; P: row phases (1, 2);
+// XCH: the epilogue stores into the exchange buffers instead of out.
 // One CTA per SM (16 consumer warps take the SM's registers).
-template <int NT, int WS, int P>
+template <int NT, int WS, int P, bool XCH>
 __global__ void __launch_bounds__((kCW + 1) * 32, 1)
     k_gemm_int4(const __grid_constant__ WMaps maps, const GemmParams p) {
   using L = Layout<WS, P>;
@@ -554,7 +563,22 @@ __global__ void __launch_bounds__((kCW + 1) * 32, 1)
       sum.z += v.z;
       sum.w += v.w;
     }
-    store_half4(p.out + static_cast<size_t>(n) * p.M + c0 + gf * 32 + 4 * c4, sum.x, sum.y, sum.z, sum.w);
+    if constexpr (XCH) {
+      // the same fp16 rounding as the stored output; the epoch was advanced by the
+      // previous join of this channel, which completed before pdl_wait above returned
+      const int row = p.xrow0 + n;
+      const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(p.xstate + row) + 1u;
+      const __half2 lo = __floats2half2_rn(sum.x, sum.y), hi = __floats2half2_rn(sum.z, sum.w);
+      const uint32_t wlo = *reinterpret_cast<const uint32_t*>(&lo), whi = *reinterpret_cast<const uint32_t*>(&hi);
+      const long long e = static_cast<long long>(row) * p.M + c0 + gf * 32 + 4 * c4;  // even word pair
+      for (int r = 0; r < p.xworld; ++r) {
+        uint2* d = peer_row_slot(p.xbuf[r], static_cast<int>(epoch & 1u), p.xrank, p.xslot) + e / 2;
+        st_ll(d, wlo, epoch);
+        st_ll(d + 1, whi, epoch);
+      }
+    } else {
+      store_half4(p.out + static_cast<size_t>(n) * p.M + c0 + gf * 32 + 4 * c4, sum.x, sum.y, sum.z, sum.w);
+    }
   }
 }
 
@@ -654,7 +678,7 @@ static Plan make_plan(int N, int KS, int P, int ws, int ck) {
 
 template <int NT, int WS, int P>
 static int max_clusters_q(int ck, int smem) {
-  auto kern = k_gemm_int4<NT, WS, P>;
+  auto kern = k_gemm_int4<NT, WS, P, false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) {
     (void)cudaGetLastError();
     return -1;
@@ -823,10 +847,11 @@ static bool weight_maps(const uint8_t* sb, int K, int M, WMaps* maps) {
   return true;
 }
 
-template <int NT, int WS, int P>
+// x: the exchange of an XCH launch (its fields of GemmParams), else null.
+template <int NT, int WS, int P, bool XCH>
 static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M,
-                       uint32_t* err, cudaStream_t st) {
-  auto kern = k_gemm_int4<NT, WS, P>;
+                       uint32_t* err, cudaStream_t st, const GemmParams* x) {
+  auto kern = k_gemm_int4<NT, WS, P, XCH>;
   static bool attr_set[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MB_ERR_LAUNCH;
@@ -840,6 +865,19 @@ static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, u
   WMaps maps;
   if (!weight_maps<WS, P>(sb, K, M, &maps)) return MB_ERR_LAUNCH;
   GemmParams prm;
+  if (XCH) {
+    for (int r = 0; r < kPeerMaxRanks; ++r) prm.xbuf[r] = x->xbuf[r];
+    prm.xstate = x->xstate;
+    prm.xslot = x->xslot;
+    prm.xworld = x->xworld;
+    prm.xrank = x->xrank;
+    prm.xrow0 = x->xrow0;
+  } else {
+    for (int r = 0; r < kPeerMaxRanks; ++r) prm.xbuf[r] = nullptr;
+    prm.xstate = nullptr;
+    prm.xslot = 0;
+    prm.xworld = prm.xrank = prm.xrow0 = 0;
+  }
   prm.out = out;
   prm.act = act;
   prm.err = err;
@@ -885,13 +923,13 @@ static int launch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, u
   return launch_status();
 }
 
-template <int NT>
+template <int NT, bool XCH = false>
 static int dispatch_fast(const Plan& pl, const uint16_t* act, const uint8_t* sb, uint16_t* out, int N, int K, int M,
-                         uint32_t* err, cudaStream_t st) {
-  if (pl.ws == 256) return launch_fast<NT, 256, 1>(pl, act, sb, out, N, K, M, err, st);
+                         uint32_t* err, cudaStream_t st, const GemmParams* x = nullptr) {
+  if (pl.ws == 256) return launch_fast<NT, 256, 1, XCH>(pl, act, sb, out, N, K, M, err, st, x);
   if (pl.ws == 128)
-    return pl.P == 1 ? launch_fast<NT, 128, 1>(pl, act, sb, out, N, K, M, err, st)
-                     : launch_fast<NT, 128, 2>(pl, act, sb, out, N, K, M, err, st);
+    return pl.P == 1 ? launch_fast<NT, 128, 1, XCH>(pl, act, sb, out, N, K, M, err, st, x)
+                     : launch_fast<NT, 128, 2, XCH>(pl, act, sb, out, N, K, M, err, st, x);
   return MB_ERR_UNSUPPORTED;
 }
 
@@ -943,6 +981,40 @@ extern "C" {
 int32_t mb_int4_gemm(const uint16_t* act, const uint8_t* sb, uint16_t* out, int32_t N, int32_t K, int32_t M,
                      uint32_t* dev_err, void* stream) {
   return gemm_all(act, sb, out, N, K, M, dev_err, stream);
+}
+
+int32_t mb_int4_gemm_peer(const uint16_t* act, const uint8_t* sb, int32_t N, int32_t K, int32_t M,
+                          void* const* bufs, int32_t world, int32_t rank, int64_t slot_elems, const uint32_t* state,
+                          uint32_t* dev_err, void* stream) {
+  if (!act || !sb || !bufs || !state) return MB_ERR_NULL;
+  if (N < 1 || N > kPeerMaxRows || K < 1 || M < 8 || M % 8 != 0 || (static_cast<int64_t>(K) * M) % 256 != 0 ||
+      world < 1 || world > kPeerMaxRanks || rank < 0 || rank >= world || slot_elems % 8 != 0 ||
+      static_cast<int64_t>(N) * M > slot_elems)
+    return MB_ERR_ARGS;
+  GemmParams x;
+  for (int r = 0; r < kPeerMaxRanks; ++r) {
+    x.xbuf[r] = r < world ? static_cast<uint8_t*>(bufs[r]) : nullptr;
+    if (r < world && (!bufs[r] || !aligned(bufs[r], 256))) return MB_ERR_ARGS;
+  }
+  if (!aligned(act, 16) || !aligned(sb, 16)) return MB_ERR_UNSUPPORTED;  // the fast plan only
+  x.xstate = state;
+  x.xslot = slot_elems;
+  x.xworld = world;
+  x.xrank = rank;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int r0 = 0; r0 < N; r0 += 32)  // every block on the fast plan before anything is launched
+    if (!plan_gemm(std::min(32, N - r0), K, M, sm_count()).fast) return MB_ERR_UNSUPPORTED;
+  for (int r0 = 0; r0 < N; r0 += 32) {
+    const int nb = std::min(32, N - r0);
+    const Plan pl = plan_gemm(nb, K, M, sm_count());
+    x.xrow0 = r0;
+    const uint16_t* a = act + static_cast<size_t>(r0) * K;
+    const int rc = pl.nt == 1   ? dispatch_fast<1, true>(pl, a, sb, nullptr, nb, K, M, dev_err, st, &x)
+                   : pl.nt == 2 ? dispatch_fast<2, true>(pl, a, sb, nullptr, nb, K, M, dev_err, st, &x)
+                                : dispatch_fast<4, true>(pl, a, sb, nullptr, nb, K, M, dev_err, st, &x);
+    if (rc != MB_OK) return rc;
+  }
+  return MB_OK;
 }
 
 int32_t mb_int4_gemm_host(const uint16_t* act_host, const uint8_t* sb, uint16_t* out_host, int32_t N, int32_t K,

@@ -7,12 +7,15 @@
 // (batch_generator.py:203-206, 224-227). Instead of a library all-reduce followed by
 // separate kernels, each exchange here is ONE kernel per rank that stores its rows
 // straight into the other ranks' exchange buffers (plain peer stores over NVLink, no
-// multicast), publishes them with a release flag, waits (bounded) for every rank's
-// rows and finishes the operation locally:
+// multicast), waits (bounded) for every rank's rows and finishes the operation
+// locally:
 //   k_peer_add_rmsnorm : sum the N x D partials in rank order in fp32, round to fp16
 //                        (the all-reduced projection), x += it, h = RMSNorm(x) * w;
 //   k_peer_argmax      : best (value, column) key of this rank's logits row, exchanged,
 //                        integer max over ranks -> token id.
+// When the projection is the fused GEMM of mb_int4_gemm_peer (gemm.cu), its epilogue
+// has already stored this rank's rows as exchange words, and the join
+// (k_peer_add_rmsnorm<true>, mb_peer_sum_rmsnorm) only waits, sums and normalises.
 // Every rank sums the same values in the same order, so the residual streams stay
 // bit-identical across ranks.
 //
@@ -20,11 +23,8 @@
 // by the other ranks with 8-byte "low-latency" words: 4 bytes of payload and 4 bytes
 // holding the epoch of the call that wrote them, stored in one transaction, so a
 // receiver that reads a word carrying the current epoch has its payload too (no fence,
-// no separate flag, one NVLink crossing per word):
-//   [0, 16384)      channel 1 (argmax): [2 parities][kMaxRanks][kMaxRows] keys, each
-//                   two words (low and high 32 bits of the 64-bit key)
-//   [16384, ...)    channel 0 (add_rmsnorm) rows: [2 parities][kMaxRanks][slot_elems / 2]
-//                   words, two fp16 per word
+// no separate flag, one NVLink crossing per word). Layout in peer_ll.cuh: channel 1
+// holds the argmax keys, channel 0 the rows of the residual joins.
 // Epoch e (1, 2, ...) of a channel writes parity e & 1; a rank can only reach epoch
 // e + 2 after every rank has finished epoch e + 1, hence finished reading epoch e's
 // parity, so two parities never race. Each row's epoch lives in a small local state
@@ -46,15 +46,11 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "peer_ll.cuh"
 
 namespace mb {
 
-constexpr int kPeerMaxRanks = 8;
-constexpr int kPeerMaxRows = 64;
 constexpr int kPeerBlock = 256;
-constexpr size_t kPeerKeyOff = 0;
-constexpr size_t kPeerRowOff = 16384;
-static_assert(kPeerKeyOff + 2 * kPeerMaxRanks * kPeerMaxRows * 2 * sizeof(uint2) <= kPeerRowOff, "layout");
 
 struct PeerSet {
   uint8_t* buf[kPeerMaxRanks];  // every rank's exchange buffer as mapped in this process (own included)
@@ -68,17 +64,6 @@ __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
-}
-
-// One low-latency word: payload and epoch in a single 8-byte store / load.
-__device__ __forceinline__ void st_ll(uint2* p, uint32_t payload, uint32_t epoch) {
-  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(payload), "r"(epoch) : "memory");
-}
-
-__device__ __forceinline__ uint2 ld_ll(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-  return v;
 }
 
 // The payload of word `p` once it carries `epoch`; waits at most until `deadline`
@@ -118,7 +103,9 @@ __device__ __forceinline__ float block_sum_fixed(float v, float* part) {
   return tot;
 }
 
-// One CTA per row n. state = the rows' epochs of channel 0.
+// One CTA per row n. state = the rows' epochs of channel 0. STORED: every rank's rows
+// of this epoch were stored by its GEMM's epilogue (partial unused).
+template <bool STORED>
 __global__ void __launch_bounds__(kPeerBlock) k_peer_add_rmsnorm(PeerSet ps, const uint16_t* __restrict__ partial,
                                                                  float* __restrict__ x, const float* __restrict__ w,
                                                                  int D, float eps, uint16_t* __restrict__ h,
@@ -143,19 +130,20 @@ __global__ void __launch_bounds__(kPeerBlock) k_peer_add_rmsnorm(PeerSet ps, con
     wv[j] = c < D ? w[c] : 0.0f;
   }
   auto slot = [&](uint8_t* buf, int src) {
-    return reinterpret_cast<uint2*>(buf + kPeerRowOff) +
-           ((static_cast<int64_t>(par) * kPeerMaxRanks + src) * ps.slot_elems + static_cast<int64_t>(n) * D) / 2;
+    return peer_row_slot(buf, par, src, ps.slot_elems) + static_cast<int64_t>(n) * D / 2;
   };
   // 1. this rank's row n as low-latency words into slot [par][rank] of every rank
-  const uint4* src = reinterpret_cast<const uint4*>(partial + static_cast<int64_t>(n) * D);
-  for (int i = threadIdx.x; i < chunks; i += kPeerBlock) {
-    const uint4 v = src[i];
-    for (int q = 0; q < ps.world; ++q) {
-      uint2* d = slot(ps.buf[q], ps.rank) + 4 * i;
-      st_ll(d, v.x, epoch);
-      st_ll(d + 1, v.y, epoch);
-      st_ll(d + 2, v.z, epoch);
-      st_ll(d + 3, v.w, epoch);
+  if constexpr (!STORED) {
+    const uint4* src = reinterpret_cast<const uint4*>(partial + static_cast<int64_t>(n) * D);
+    for (int i = threadIdx.x; i < chunks; i += kPeerBlock) {
+      const uint4 v = src[i];
+      for (int q = 0; q < ps.world; ++q) {
+        uint2* d = slot(ps.buf[q], ps.rank) + 4 * i;
+        st_ll(d, v.x, epoch);
+        st_ll(d + 1, v.y, epoch);
+        st_ll(d + 2, v.z, epoch);
+        st_ll(d + 3, v.w, epoch);
+      }
     }
   }
   // 2. every rank's words of the same chunks (own buffer), summed in rank order in fp32,
@@ -335,23 +323,44 @@ int32_t mb_ipc_free(void* ptr) {
   return MB_OK;
 }
 
+static int32_t peer_join(void* const* bufs, int32_t world, int32_t rank, int64_t slot_elems, int64_t timeout_ns,
+                         const uint16_t* partial, float* x, const float* w, int32_t N, int32_t D, float eps,
+                         uint16_t* h, uint32_t* state, uint32_t* dev_err, void* stream) {
+  if (N < 1 || N > kPeerMaxRows || D < 8 || D % 8 != 0 || static_cast<int64_t>(N) * D > slot_elems ||
+      D > 16384)
+    return MB_ERR_ARGS;
+  if (partial && !aligned(partial, 16)) return MB_ERR_ALIGN;
+  PeerSet ps;
+  if (!make_peer_set(bufs, world, rank, slot_elems, timeout_ns, &ps)) return MB_ERR_ARGS;
+  const size_t smem = static_cast<size_t>(D) * sizeof(float);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (partial) {
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(k_peer_add_rmsnorm<false>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(smem)) != cudaSuccess)
+      return MB_ERR_LAUNCH;
+    return launch_with_pdl(k_peer_add_rmsnorm<false>, dim3(N), dim3(kPeerBlock), smem, st, ps, partial, x, w, D,
+                           eps, h, state, dev_err);
+  }
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(k_peer_add_rmsnorm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(smem)) != cudaSuccess)
+    return MB_ERR_LAUNCH;
+  return launch_with_pdl(k_peer_add_rmsnorm<true>, dim3(N), dim3(kPeerBlock), smem, st, ps, partial, x, w, D, eps, h,
+                         state, dev_err);
+}
+
 int32_t mb_peer_add_rmsnorm(void* const* bufs, int32_t world, int32_t rank, int64_t slot_elems, int64_t timeout_ns,
                             const uint16_t* partial, float* x, const float* w, int32_t N, int32_t D, float eps,
                             uint16_t* h, uint32_t* state, uint32_t* dev_err, void* stream) {
   if (!bufs || !partial || !x || !w || !h || !state) return MB_ERR_NULL;
-  if (N < 1 || N > kPeerMaxRows || D < 8 || D % 8 != 0 || static_cast<int64_t>(N) * D > slot_elems ||
-      D > 16384)
-    return MB_ERR_ARGS;
-  if (!aligned(partial, 16)) return MB_ERR_ALIGN;
-  PeerSet ps;
-  if (!make_peer_set(bufs, world, rank, slot_elems, timeout_ns, &ps)) return MB_ERR_ARGS;
-  const size_t smem = static_cast<size_t>(D) * sizeof(float);
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(k_peer_add_rmsnorm, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-          cudaSuccess)
-    return MB_ERR_LAUNCH;
-  return launch_with_pdl(k_peer_add_rmsnorm, dim3(N), dim3(kPeerBlock), smem, static_cast<cudaStream_t>(stream), ps,
-                         partial, x, w, D, eps, h, state, dev_err);
+  return peer_join(bufs, world, rank, slot_elems, timeout_ns, partial, x, w, N, D, eps, h, state, dev_err, stream);
+}
+
+int32_t mb_peer_sum_rmsnorm(void* const* bufs, int32_t world, int32_t rank, int64_t slot_elems, int64_t timeout_ns,
+                            float* x, const float* w, int32_t N, int32_t D, float eps, uint16_t* h, uint32_t* state,
+                            uint32_t* dev_err, void* stream) {
+  if (!bufs || !x || !w || !h || !state) return MB_ERR_NULL;
+  return peer_join(bufs, world, rank, slot_elems, timeout_ns, nullptr, x, w, N, D, eps, h, state, dev_err, stream);
 }
 
 int32_t mb_peer_argmax(void* const* bufs, int32_t world, int32_t rank, int64_t slot_elems, int64_t timeout_ns,

@@ -23,10 +23,13 @@ Tensor parallelism (``rank``/``world``, one process per GPU): the Megatron split
 columns and down rows of an FFN range; lm_head columns of a vocabulary range. Every
 rank draws the whole weights from the same random stream as one GPU and keeps its
 slice, so the shards hold exactly the one-GPU model's codes and scales. The two
-row-parallel partial products of a layer are joined by ``exchange="peer"`` (one
-kernel per join: peer stores over NVLink, then the residual add and RMSNorm; the
-default) or ``"nccl"`` (``all_reduce``, then ``mb_add_rmsnorm``); the greedy choice
-over the split vocabulary is one 64-bit key per shard, maximised across ranks.
+row-parallel partial products of a layer are joined by ``exchange="peer"`` (the
+default: the o_proj and down GEMMs store their rows into every rank's exchange buffer
+from their epilogue, ``mb_int4_gemm_peer``, and one kernel per join waits for the
+other ranks' rows over NVLink, then does the residual add and RMSNorm;
+``fused_join=False`` keeps the GEMM's partial in HBM and lets the join kernel store
+it) or ``"nccl"`` (``all_reduce``, then ``mb_add_rmsnorm``); the greedy choice over
+the split vocabulary is one 64-bit key per shard, maximised across ranks.
 
 ``temperature > 0`` replaces the greedy choice by ``mb_sample_tokens``: a draw from
 the top-50 of the exp-LUT softmax of the scaled logits, as the reference's
@@ -45,6 +48,9 @@ import numpy as np
 
 from . import _lib
 from ._lib import check, lib, stream_of
+
+
+_STORED = object()  # a row-parallel partial that its GEMM stored into the exchange buffers
 
 
 @dataclass
@@ -95,7 +101,8 @@ class Int4Decoder:
 
     def __init__(self, cfg: DecoderConfig, n_traces: int, device="cuda:0", seed: int = 0, std: float = 0.02,
                  keep_dense: bool = False, rank: int = 0, world: int = 1, group=None, exchange: str = "peer",
-                 exchange_timeout_s: float = 10.0, temperature: float = 0.0, sample_seed: int = 0):
+                 exchange_timeout_s: float = 10.0, temperature: float = 0.0, sample_seed: int = 0,
+                 fused_join: bool = True):
         t = _lib.require_cuda()
         from .attention import ExponentialLUT
         from .dequant import quantize_to_superblocks
@@ -110,6 +117,7 @@ class Int4Decoder:
             raise ValueError("exchange must be 'peer' or 'nccl'")
         self.rank, self.world, self.group = rank, world, group
         self.exchange, self.peer, self.exchange_timeout_s = exchange, None, exchange_timeout_s
+        self.fused_join = bool(fused_join) and world > 1 and exchange == "peer"
         self.temperature = float(temperature)
         self.shards = tp_shards(cfg, world)
         sh = {k: v[rank] for k, v in self.shards.items()}
@@ -326,10 +334,23 @@ class Int4Decoder:
             self.peer.close()
             self.peer = None
 
+    def _row_parallel(self, act, w, K, st):
+        """This rank's partial of a row-parallel projection (o_proj, down). With the
+        fused join the GEMM's epilogue stores it into the exchange buffers and the
+        marker ``_STORED`` is returned; otherwise it lands in ``self.o``."""
+        if self.fused_join and self.peer.gemm(act, w, K, self.cfg.hidden, self.err, st):
+            return _STORED
+        check(lib().mb_int4_gemm(act.data_ptr(), w.data_ptr(), self.o.data_ptr(), self.N, K, self.cfg.hidden,
+                                 self.err.data_ptr(), st), "row-parallel GEMM")
+        return self.o
+
     def _residual_norm(self, y, w, st):
         """x += y (the sum over ranks of the row-parallel partials y), h = RMSNorm(x) * w."""
         cfg, N, L = self.cfg, self.N, lib()
         p = lambda x: x.data_ptr()  # noqa: E731
+        if y is _STORED:  # every rank's rows are in the exchange buffers already
+            self.peer.sum_rmsnorm(self.x, w, cfg.eps, self.h, self.err, st)
+            return
         if y is not None and self.world > 1:
             if self.exchange == "peer":
                 self.peer.add_rmsnorm(y, self.x, w, cfg.eps, self.h, self.err, st)
@@ -365,12 +386,11 @@ class Int4Decoder:
                                              self.length + 1, cfg.max_len, dh, self.scale, p(self.table),
                                              self.lut.size, float(self.lut.range_max), p(self.ws), self.ws.numel(),
                                              st), "mb_decode_attn_cache")
-            check(L.mb_int4_gemm(p(self.att), p(lw["wo"]), p(self.o), N, Dl, D, err, st), "o_proj")
-            self._residual_norm(self.o, lw["ffn_norm"], st)  # row-parallel o_proj joined over ranks
+            y = self._row_parallel(self.att, lw["wo"], Dl, st)  # o_proj
+            self._residual_norm(y, lw["ffn_norm"], st)  # row-parallel o_proj joined over ranks
             check(L.mb_int4_gemm(p(self.h), p(lw["wgu"]), p(self.gu), N, D, 2 * F, err, st), "gate_up")
             check(L.mb_swiglu(p(self.gu), N, F, p(self.a), st), "mb_swiglu")
-            check(L.mb_int4_gemm(p(self.a), p(lw["wd"]), p(self.o), N, F, D, err, st), "down")
-            y = self.o  # row-parallel down projection, joined by the next norm
+            y = self._row_parallel(self.a, lw["wd"], F, st)  # down, joined by the next norm
         self._residual_norm(y, self.final_norm, st)
         check(L.mb_int4_gemm(p(self.h), p(self.lm_head), p(self.logits), N, D, V, err, st), "lm_head")
         if self.sampler is not None:

@@ -7,6 +7,8 @@ its rows into the peers' buffers and waits, bounded, for theirs (``mb_peer_add_r
 and ``mb_peer_argmax`` in ``include/moat_b200.h``). They replace, on the decode path, a
 library all-reduce of the row-parallel partial products followed by the residual add
 and RMSNorm, and the all-reduce of the greedy keys of a column-split vocabulary.
+``gemm`` + ``sum_rmsnorm`` fuse the row-parallel projection with its join: the GEMM's
+epilogue stores the rows into the exchange buffers itself (``mb_int4_gemm_peer``).
 
 Every rank must make the same calls in the same order, on its own GPU: the exchange
 refuses a group in which two ranks share a device, because the two kernels that wait
@@ -24,6 +26,7 @@ from ._lib import check, lib, stream_of
 
 HANDLE_BYTES = 64
 DEVERR_TIMEOUT = 1
+ERR_UNSUPPORTED = -6  # MB_ERR_UNSUPPORTED
 STATE_WORDS = 64  # MB_PEER_STATE_WORDS: one epoch word per row and exchange kind
 
 
@@ -94,6 +97,30 @@ class PeerExchange:
                                         partial.data_ptr(), x.data_ptr(), w.data_ptr(), N, D, float(eps),
                                         h.data_ptr(), self.state.data_ptr(), err.data_ptr(), st),
               "mb_peer_add_rmsnorm")
+
+    def gemm(self, act, sb, K: int, M: int, err, stream: Optional[int] = None):
+        """This rank's row-parallel partial ``act [N, K] x int4 sb [K, M]`` (M = D),
+        stored by the GEMM's epilogue straight into every rank's exchange buffer; the
+        next call must be ``sum_rmsnorm`` (``mb_int4_gemm_peer``). Returns False, having
+        launched nothing, for a shape off the fast GEMM plan."""
+        N = act.shape[0]
+        st = stream_of(self.dev) if stream is None else stream
+        rc = lib().mb_int4_gemm_peer(act.data_ptr(), sb.data_ptr(), N, K, M, self._bufs, self.world, self.rank,
+                                     self.slot_elems, self.state.data_ptr(), err.data_ptr(), st)
+        if rc == ERR_UNSUPPORTED:
+            return False
+        check(rc, "mb_int4_gemm_peer")
+        return True
+
+    def sum_rmsnorm(self, x, w, eps: float, h, err, stream: Optional[int] = None):
+        """The join after ``gemm``: x += fp16(sum over ranks of the stored rows),
+        h = RMSNorm(x) * w."""
+        N, D = x.shape
+        st = stream_of(self.dev) if stream is None else stream
+        check(lib().mb_peer_sum_rmsnorm(self._bufs, self.world, self.rank, self.slot_elems, self.timeout_ns,
+                                        x.data_ptr(), w.data_ptr(), N, D, float(eps), h.data_ptr(),
+                                        self.state.data_ptr(), err.data_ptr(), st),
+              "mb_peer_sum_rmsnorm")
 
     def argmax(self, logits, col0: int, ids, err, stream: Optional[int] = None):
         """ids = the global greedy choice over every rank's column range of the logits."""

@@ -149,6 +149,15 @@ def test_tensor_parallel_and_sampling_entries_validate_on_the_host(L):
                                  None) == -2
     assert L.mb_peer_add_rmsnorm(bufs, 9, 0, 4096, 10**9, fake, fake, fake, 2, 2048, 1e-6, fake, fake, None,
                                  None) == -2
+    # the row-parallel GEMM that stores into the exchange buffers, and its join
+    assert L.mb_int4_gemm_peer(fake, fake, 16, 1024, 2048, bufs, 2, 0, 16 * 2048, None, None, None) == -1
+    assert L.mb_int4_gemm_peer(fake, fake, 65, 1024, 2048, bufs, 2, 0, 65 * 2048, fake, None, None) == -2
+    assert L.mb_int4_gemm_peer(fake, fake, 16, 1024, 2048, bufs, 2, 0, 2048, fake, None, None) == -2  # slot
+    assert L.mb_int4_gemm_peer(fake, fake, 16, 1024, 2048, bufs, 2, 2, 16 * 2048, fake, None, None) == -2
+    assert L.mb_int4_gemm_peer(ctypes.c_void_p(0x10008), fake, 16, 1024, 2048, bufs, 2, 0, 16 * 2048, fake, None,
+                               None) == -6  # unaligned activations: off the fast plan
+    assert L.mb_peer_sum_rmsnorm(bufs, 2, 0, 4096, 10**9, None, fake, 2, 2048, 1e-6, fake, fake, None, None) == -1
+    assert L.mb_peer_sum_rmsnorm(bufs, 2, 0, 2048, 10**9, fake, fake, 2, 2048, 1e-6, fake, fake, None, None) == -2
     assert L.mb_peer_argmax(bufs, 2, 0, 4096, 0, fake, 2, 10, 0, fake, fake, None, None) == -2   # no timeout
     assert L.mb_peer_argmax(bufs, 2, 0, 4096, 10**9, fake, 2, 10, 0, None, fake, None, None) == -1
     # sampler: sizes, workspace, top_k range, dtype flag

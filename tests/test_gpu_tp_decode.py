@@ -6,9 +6,11 @@
   o_proj rows of its heads, gate/up columns and down rows of its FFN range, lm_head
   columns of its vocabulary range (whole groups, so identical codes and scales).
 * The NVLink peer exchange on one GPU: with one rank it equals ``mb_add_rmsnorm`` and
-  ``mb_argmax_f16`` bit for bit over several epochs; a peer that never delivers makes
-  the bounded wait expire into the error word.
-* Two ranks (needs 2 GPUs), joined by the NVLink peer exchange or by NCCL: eager and
+  ``mb_argmax_f16`` bit for bit over several epochs, and so does the row-parallel GEMM
+  whose epilogue stores its rows into the exchange buffers followed by the join over
+  them; a peer that never delivers makes the bounded wait expire into the error word.
+* Two ranks (needs 2 GPUs), joined by the NVLink peer exchange (fused into the GEMM or
+  not) or by NCCL: eager and
   graph-captured TP steps against the one-GPU decoder fed the same token ids. Logits
   within 2e-2 (the row-parallel partial products are rounded to fp16 before they are
   summed, instead of one fp32 accumulation); the residual stream identical on both
@@ -143,6 +145,53 @@ def test_peer_exchange_one_rank_equals_local_kernels(cuda):
     assert epochs[:N] == [5] * N and epochs[64:64 + N] == [5] * N and not any(epochs[N:64] + epochs[64 + N:])
 
 
+@pytest.mark.parametrize("N", [16, 40])
+def test_fused_gemm_join_one_rank_equals_local_kernels(cuda, N):
+    """world = 1: the row-parallel GEMM whose epilogue stores its rows as exchange words
+    (mb_int4_gemm_peer), then the join over the stored rows (mb_peer_sum_rmsnorm), give
+    x and h bit for bit as mb_int4_gemm + mb_add_rmsnorm, over six epochs (both
+    parities) alternating with the unfused peer join on the same epoch state. N = 40
+    runs the GEMM as two launches (32 + 8 batch rows)."""
+    import torch
+    from moat_b200._lib import lib
+    from moat_b200.dequant import quantize_to_superblocks
+    L = lib()
+    K, D = 1024, 2048
+    g = torch.Generator(device=cuda)
+    g.manual_seed(5)
+    sb = quantize_to_superblocks((0.02 * torch.randn((K, D), generator=g, device=cuda)).reshape(-1))
+    bufs = _exchange_buffers(cuda, 1, 64, D)
+    slot = 64 * D
+    state = torch.zeros(128, dtype=torch.int32, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    x_a = torch.randn((N, D), generator=g, device=cuda)
+    x_b = x_a.clone()
+    w = 1.0 + 0.1 * torch.randn(D, generator=g, device=cuda)
+    h_a = torch.empty((N, D), dtype=torch.float16, device=cuda)
+    h_b = torch.empty_like(h_a)
+    y = torch.empty((N, D), dtype=torch.float16, device=cuda)
+    for e in range(6):
+        act = torch.randn((N, K), generator=g, device=cuda).half()
+        assert L.mb_int4_gemm(act.data_ptr(), sb.data_ptr(), y.data_ptr(), N, K, D, err.data_ptr(), _st()) == 0
+        if e % 2 == 0:
+            assert L.mb_int4_gemm_peer(act.data_ptr(), sb.data_ptr(), N, K, D, _ptrs(bufs), 1, 0, slot,
+                                       state.data_ptr(), err.data_ptr(), _st()) == 0
+            assert L.mb_peer_sum_rmsnorm(_ptrs(bufs), 1, 0, slot, 10**9, x_a.data_ptr(), w.data_ptr(), N, D, 1e-6,
+                                         h_a.data_ptr(), state.data_ptr(), err.data_ptr(), _st()) == 0
+        else:
+            assert L.mb_peer_add_rmsnorm(_ptrs(bufs), 1, 0, slot, 10**9, y.data_ptr(), x_a.data_ptr(),
+                                         w.data_ptr(), N, D, 1e-6, h_a.data_ptr(), state.data_ptr(),
+                                         err.data_ptr(), _st()) == 0
+        assert L.mb_add_rmsnorm(x_b.data_ptr(), y.data_ptr(), w.data_ptr(), N, D, 1e-6, h_b.data_ptr(), _st()) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(x_a, x_b) and torch.equal(h_a, h_b), e
+    assert int(err.item()) == 0
+    assert state.cpu().tolist()[:N] == [6] * N
+    # off the fast plan (M % 128 != 0): refused before any launch
+    assert L.mb_int4_gemm_peer(act.data_ptr(), sb.data_ptr(), N, 2048, 1000 // 8 * 8, _ptrs(bufs), 1, 0, slot,
+                               state.data_ptr(), err.data_ptr(), _st()) == -6
+
+
 def test_peer_wait_gives_up_with_error_bit(cuda):
     """A rank whose peer never delivers (a second buffer whose flags nothing sets):
     the bounded wait expires, the kernel sets MB_DEVERR_TIMEOUT and returns, and the
@@ -221,7 +270,8 @@ def _tp_worker(rank, world, port, exchange, q):
     tp = one = None
     try:
         cfg, N = _small_cfg(), 4
-        tp = Int4Decoder(cfg, N, device=dev, seed=11, rank=rank, world=world, exchange=exchange,
+        tp = Int4Decoder(cfg, N, device=dev, seed=11, rank=rank, world=world,
+                         exchange="nccl" if exchange == "nccl" else "peer", fused_join=exchange != "peer_unfused",
                          exchange_timeout_s=2.0)
         tp.fill_prompt_cache(20, seed=12)
         if rank == 0:
@@ -260,7 +310,7 @@ def _tp_worker(rank, world, port, exchange, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+@pytest.mark.parametrize("exchange", ["peer", "peer_unfused", "nccl"])
 def test_tp_decode_two_gpus_matches_one_gpu(exchange):
     _needs_two_gpus()
     res = _spawn(_tp_worker, 2, exchange)
@@ -340,6 +390,66 @@ def test_peer_exchange_two_gpus_matches_numpy():
         ref_ids = S.reference_argmax(a["logits"])
         assert a["ids"].tolist() == ref_ids.tolist() == b["ids"].tolist()
         assert ref_ids[s] == 5
+    assert res[0]["err"] == 0 and res[1]["err"] == 0
+
+
+def _fused_join_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from moat_b200.dequant import quantize_to_superblocks
+    from moat_b200.gemm import batched_gemm
+    from moat_b200.peer import PeerExchange
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    px = None
+    try:
+        N, K, D = 16, 1024, 2048
+        px = PeerExchange(N, D, dev, timeout_s=2.0)
+        rng = np.random.default_rng(200 + rank)
+        sb = quantize_to_superblocks(torch.from_numpy((0.02 * rng.standard_normal(K * D)).astype(np.float32)).to(dev))
+        x0 = np.random.default_rng(300).standard_normal((N, D)).astype(np.float32)
+        w = torch.ones(D, device=dev)
+        x = torch.from_numpy(x0).to(dev)
+        h = torch.empty((N, D), dtype=torch.float16, device=dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        out = []
+        for step in range(4):
+            act = torch.from_numpy(rng.standard_normal((N, K)).astype(np.float16)).to(dev)
+            y = batched_gemm(act, sb, K, D)  # this rank's partial, unfused, for the check
+            if step % 2 == 0:
+                assert px.gemm(act, sb, K, D, err)
+                px.sum_rmsnorm(x, w, 1e-6, h, err)
+            else:
+                px.add_rmsnorm(y, x, w, 1e-6, h, err)
+            torch.cuda.synchronize()
+            out.append({"x": x.cpu().numpy(), "h": h.float().cpu().numpy(), "y": y.cpu().numpy()})
+        q.put((rank, {"steps": out, "x0": x0, "err": int(err.item())}))
+    except Exception as e:
+        q.put((rank, repr(e)))
+    finally:
+        if px is not None:
+            px.close()
+        dist.destroy_process_group()
+
+
+def test_fused_gemm_join_two_gpus_matches_numpy():
+    """Two ranks, alternating the fused row-parallel GEMM + join (epochs 1, 3) with the
+    unfused peer join (2, 4): x += fp16(Y_0 + Y_1 summed in fp32), with Y_r rank r's
+    own mb_int4_gemm partial, bit for bit on both ranks; identical h on both ranks."""
+    _needs_two_gpus()
+    res = _spawn(_fused_join_worker, 2)
+    x = res[0]["x0"].copy()
+    for s in range(4):
+        a, b = res[0]["steps"][s], res[1]["steps"][s]
+        d = (a["y"].astype(np.float32) + b["y"].astype(np.float32)).astype(np.float16)
+        x = x + d.astype(np.float32)
+        np.testing.assert_array_equal(a["x"], x, err_msg=f"step {s}")
+        np.testing.assert_array_equal(b["x"], x, err_msg=f"step {s}")
+        np.testing.assert_array_equal(a["h"], b["h"])
     assert res[0]["err"] == 0 and res[1]["err"] == 0
 
 
