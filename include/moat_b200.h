@@ -107,7 +107,8 @@ int32_t mb_lut_gather_f16(const int32_t* idx, int64_t n, const uint16_t* lut, in
  * buffers act/weights/out/N/K/M) and fused_batched_gemm_int4 (:116-169), whose CPU
  * form is the decode step's `activations @ W` (batch_generator.py:290).
  * Requires K*M % 256 == 0 and N >= 1; any N (rows are processed in blocks of 32
- * per launch). No scratch memory: split-K partial sums are reduced on chip.
+ * per launch, or of 16 where only 16 rows fit the fast plan's shared memory). No
+ * scratch memory: split-K partial sums are reduced on chip.
  * dev_err is an optional DEVICE word (may be NULL) that receives MB_DEVERR_* bits
  * if a bounded wait inside the kernel gives up. The fast path needs K % 8 == 0,
  * M % 128 == 0 and 16-byte aligned act / sb; other shapes take a slower path.

@@ -963,8 +963,14 @@ static int gemm_all(const uint16_t* act, const uint8_t* sb, uint16_t* out, int32
   if (N < 1 || K < 1 || M < 1 || (static_cast<int64_t>(K) * M) % 256 != 0) return MB_ERR_ARGS;
   if (!act || !sb || !out) return MB_ERR_NULL;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  for (int r0 = 0; r0 < N; r0 += 32) {
-    const int nb = std::min(32, N - r0);
+  // Rows per launch: 32, or 16 where a block of more than 16 rows does not fit the fast
+  // plan but 16 rows do (a wide matrix without a K split and a long K: the activations
+  // of the whole K for 32 rows leave no room for the ring), since two fast launches
+  // beat one of the generic kernel by far.
+  int rb = 32;
+  if (N > 16 && !plan_gemm(std::min(N, 32), K, M, sm_count()).fast && plan_gemm(16, K, M, sm_count()).fast) rb = 16;
+  for (int r0 = 0; r0 < N; r0 += rb) {
+    const int nb = std::min(rb, N - r0);
     const int rc = gemm_rows(act + static_cast<size_t>(r0) * K, sb, out + static_cast<size_t>(r0) * M, nb, K, M,
                              dev_err, st);
     if (rc != MB_OK) return rc;

@@ -74,6 +74,44 @@ def test_ragged_shapes(cuda, N, K, M):
     close(run(x, st, K, M), O.gemm(x, w))
 
 
+_WIDE = {}
+
+
+def _wide(K, M):
+    if (K, M) not in _WIDE:
+        st = O.quantize_pack_matrix(O.make_weights(K, M, 7 + K))
+        _WIDE[(K, M)] = (st, O.unpack_superblock_weights(st).reshape(K, M))
+    return _WIDE[(K, M)]
+
+
+@pytest.mark.parametrize("K,M", [(256, 151936), (512, 76032), (520, 75904)])
+@pytest.mark.parametrize("N", [1, 16, 32])
+def test_many_strips_without_k_split(cuda, N, K, M):
+    """More strips than the GPU holds CTAs at once, and no K split: the config-5 LM head
+    (1187 strips of 128 columns) and its two tensor-parallel shards (594 and 593 strips
+    of 128) run in several waves of one CTA per strip; K = 520 ends every strip with a
+    one-slice stage. Against the oracle."""
+    from moat_b200.gemm import plan
+    pl = plan(N, K, M)
+    assert pl["kind"] == 1 and pl["cluster"] == 1 and pl["grid"] > 148, pl
+    st, w = _wide(K, M)
+    x = O.make_activations(N, K, K + N)
+    close(run(x, st, K, M), O.gemm(x, w))
+
+
+@pytest.mark.parametrize("N", [32, 40])
+def test_rows_in_blocks_of_16_where_32_do_not_fit(cuda, N):
+    """K = 2048 without a K split: the activations of the whole K for a 32-row block
+    leave no shared memory for the weight ring (the 32-row plan is not fast), so the
+    rows run as 16-row blocks of the fast kernel. Against the oracle."""
+    from moat_b200.gemm import plan
+    K, M = 2048, 19200
+    assert plan(32, K, M)["kind"] == 0 and plan(16, K, M)["kind"] == 1
+    st, w = _wide(K, M)
+    x = O.make_activations(N, K, 3 + N)
+    close(run(x, st, K, M), O.gemm(x, w))
+
+
 def test_metal_known_answers(cuda):
     """KATs of antigravity-engine/tests/test_metal_kernels.cpp restated for the INT4 path:
     byte 0x7F with scale 0.5 dequantizes to +3.5 (even) / -0.5 (odd) (:68-91), and
