@@ -773,7 +773,9 @@ def exchange_side(dev, rank: int, world: int, rows: int = 16, hidden: int = 2048
     o_proj (``[N, D / world] x [D / world, D]``) with its join: ``o_proj_gemm_join``
     (the GEMM's partial through HBM, the join kernel stores it to the peers) against
     ``o_proj_gemm_join_fused`` (the GEMM's epilogue stores its rows into the exchange
-    buffers, ``mb_int4_gemm_peer``). ``*_us``: the calls replayed from one CUDA graph,
+    buffers, ``mb_int4_gemm_peer``), and the o_proj GEMM alone (``o_proj_gemm``), so
+    that ``join_after_gemm[_fused]_us`` is what each join adds after its GEMM.
+    ``*_us``: the calls replayed from one CUDA graph,
     as in the decode step; ``*_eager_us``: launched one by one from Python
     (host-bound)."""
     import torch
@@ -831,6 +833,10 @@ def exchange_side(dev, rank: int, world: int, rows: int = 16, hidden: int = 2048
     act = torch.randn((N, Ko), generator=g, device=dev).half()
     o = torch.empty((N, D), dtype=torch.float16, device=dev)
 
+    def gemm_only():
+        st = torch.cuda.current_stream(dev).cuda_stream
+        lib().mb_int4_gemm(act.data_ptr(), wo.data_ptr(), o.data_ptr(), N, Ko, D, err.data_ptr(), st)
+
     def gemm_join():
         st = torch.cuda.current_stream(dev).cuda_stream
         lib().mb_int4_gemm(act.data_ptr(), wo.data_ptr(), o.data_ptr(), N, Ko, D, err.data_ptr(), st)
@@ -844,6 +850,7 @@ def exchange_side(dev, rank: int, world: int, rows: int = 16, hidden: int = 2048
     calls = {"add_rmsnorm": lambda: px.add_rmsnorm(partial, x, w, 1e-6, h, err),
              "argmax": lambda: px.argmax(logits, rank * Vl, ids, err),
              "nccl_all_reduce": lambda: dist.all_reduce(red),
+             "o_proj_gemm": gemm_only,
              "o_proj_gemm_join": gemm_join,
              "o_proj_gemm_join_fused": gemm_join_fused}
     try:
@@ -852,6 +859,9 @@ def exchange_side(dev, rank: int, world: int, rows: int = 16, hidden: int = 2048
             out[f"{name}_us"] = timed(fn, graph=True)
         for name, fn in calls.items():
             out[f"{name}_eager_us"] = timed(fn, graph=False)
+        # what each join adds to the o_proj GEMM it follows, as the decode step runs them
+        out["join_after_gemm_us"] = out["o_proj_gemm_join_us"] - out["o_proj_gemm_us"]
+        out["join_after_gemm_fused_us"] = out["o_proj_gemm_join_fused_us"] - out["o_proj_gemm_us"]
         e = err.clone()
         dist.all_reduce(e, op=dist.ReduceOp.MAX)
         out["device_error_bits"] = int(e.item())
