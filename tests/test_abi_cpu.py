@@ -53,6 +53,11 @@ def test_gemm_plans(L):
         assert strip in (128, 256) and M % strip == 0 and 1 <= ck <= 8
         assert grid == (M // strip) * ck and (ck == 1 or grid <= 148)
     assert L.mb_int4_gemm_plan(8, 12, 64, info) == 0 and info[0] == 0  # generic path
+    # no K split and K = 2048: 32 rows of activations over the whole K leave no room for
+    # the weight ring, 16 rows do (the GEMM then runs 16-row blocks of the fast kernel)
+    for M in (19200, 151936):
+        assert L.mb_int4_gemm_plan(32, 2048, M, info) == 0 and info[0] == 0
+        assert L.mb_int4_gemm_plan(16, 2048, M, info) == 0 and info[0] == 1 and info[2] == 1
 
 
 def test_cluster_owner_ranges():
