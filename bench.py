@@ -621,7 +621,7 @@ def decode_side(dev, rank: int = 0, world: int = 1, steps: int = 256, prompt: in
             torch.cuda.nvtx.range_pop()
         err = int(dec.err.item())
         wbytes = sum(sum(int(lw[k].numel()) for k in ("wqkv", "wo", "wgu", "wd")) for lw in dec.layers) \
-            + int(dec.lm_head.numel())
+            + int(dec.lm_head.numel()) * dec.Vl // dec.lm_cols  # without the LM head's zero padding
         kv = 2 * cfg.layers * N * dec.Hl * cfg.head_dim * 2 * (prompt + 5 + steps // 2)  # mean cache length
         tot = torch.tensor([float(wbytes + kv), float(err)], dtype=torch.float64, device=dev)
         if world > 1:

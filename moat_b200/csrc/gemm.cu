@@ -764,6 +764,16 @@ static Plan plan_gemm_uncached(int N, int K, int M, int sms) {
       }
     }
   }
+  // Without a K split and in several waves, a CTA takes about the same time per
+  // 128-row stage whatever its strip width (measured: a wave of 256-wide strips as
+  // long as one of 128-wide strips), so the wider strip halves the waves.
+  if (best.fast && best.Ck == 1 && best.ws == 128 && P == 1 && best.ctas > sms) {
+    Plan wide = make_plan(N, KS, P, 256, 1);
+    if (wide.fast) {
+      wide.ctas = M / 256;
+      best = wide;
+    }
+  }
   return best;
 }
 

@@ -130,10 +130,11 @@ class Int4Decoder:
         g.manual_seed(seed)
         self.dense = [] if keep_dense else None
 
-        def int4(K, M, cols=None, rows=None):
+        def int4(K, M, cols=None, rows=None, pad=0):
             # the whole [K, M] weight is drawn on every rank (the same random stream as
             # one GPU), then this rank's columns / rows are quantized: whole 32-wide
-            # groups, so its codes and scales equal the unsplit weight's
+            # groups, so its codes and scales equal the unsplit weight's; `pad` zero
+            # columns appended after them leave those codes and scales unchanged too
             w = t.randn((K, M), generator=g, device=self.dev, dtype=t.float32) * std
             if self.dense is not None:
                 self.dense.append(w.cpu())
@@ -141,6 +142,8 @@ class Int4Decoder:
                 w = t.cat([w[:, c0:c1] for c0, c1 in cols], dim=1)
             if rows is not None and world > 1:
                 w = w[rows[0]:rows[1]]
+            if pad:
+                w = t.cat([w, t.zeros((w.shape[0], pad), device=self.dev, dtype=w.dtype)], dim=1)
             sb = quantize_to_superblocks(w.contiguous().reshape(-1))
             del w
             return sb
@@ -156,7 +159,12 @@ class Int4Decoder:
                 "ffn_norm": (1.0 + 0.02 * t.randn((D,), generator=g, device=self.dev)).float(),
             })
         self.final_norm = (1.0 + 0.02 * t.randn((D,), generator=g, device=self.dev)).float()
-        self.lm_head = int4(D, V, cols=[(v0, v1)])
+        # The LM head streams in 256-column strips: a vocabulary range of an odd number of
+        # 128-column blocks (151,936 = 1187 x 128) gets 128 zero-weight columns, which
+        # halves the GEMM's waves (a 128-wide strip takes a wave as long as a 256-wide
+        # one); its logits are copied back to the range's own width.
+        self.lm_cols = Vl + 128 if Vl % 256 == 128 else Vl
+        self.lm_head = int4(D, V, cols=[(v0, v1)], pad=self.lm_cols - Vl)
         self.embed = (t.randn((V, D), generator=g, device=self.dev) * std).half()
         self.cs = rope_table(dh, cfg.max_len, cfg.theta).to(self.dev)
         self.lut = ExponentialLUT(range_max=cfg.lut_range)
@@ -174,6 +182,8 @@ class Int4Decoder:
         self.gu = t.empty((N, 2 * Fl), dtype=f16, device=self.dev)
         self.a = t.empty((N, Fl), dtype=f16, device=self.dev)
         self.logits = t.empty((N, Vl), dtype=f16, device=self.dev)
+        self.logits_lm = (self.logits if self.lm_cols == Vl
+                          else t.empty((N, self.lm_cols), dtype=f16, device=self.dev))
         self.keys = t.zeros((N,), dtype=t.int64, device=self.dev)
         self.ids = t.zeros((N,), dtype=t.int32, device=self.dev)
         self.logprobs = t.zeros((N,), dtype=t.float32, device=self.dev)
@@ -279,7 +289,8 @@ class Int4Decoder:
         layers = [{"wqkv": deq(lw["wqkv"], D, 3 * D), "wo": deq(lw["wo"], D, D), "wgu": deq(lw["wgu"], D, 2 * F),
                    "wd": deq(lw["wd"], F, D), "attn_norm": lw["attn_norm"].cpu(), "ffn_norm": lw["ffn_norm"].cpu()}
                   for lw in self.layers]
-        return {"layers": layers, "final_norm": self.final_norm.cpu(), "lm_head": deq(self.lm_head, D, V),
+        return {"layers": layers, "final_norm": self.final_norm.cpu(),
+                "lm_head": deq(self.lm_head, D, self.lm_cols)[:, :V].contiguous(),
                 "embed": self.embed.float().cpu(), "cis": t.view_as_complex(self.cs.cpu().contiguous())}
 
     def step(self, ids):
@@ -392,7 +403,9 @@ class Int4Decoder:
             check(L.mb_swiglu(p(self.gu), N, F, p(self.a), st), "mb_swiglu")
             y = self._row_parallel(self.a, lw["wd"], F, st)  # down, joined by the next norm
         self._residual_norm(y, self.final_norm, st)
-        check(L.mb_int4_gemm(p(self.h), p(self.lm_head), p(self.logits), N, D, V, err, st), "lm_head")
+        check(L.mb_int4_gemm(p(self.h), p(self.lm_head), p(self.logits_lm), N, D, self.lm_cols, err, st), "lm_head")
+        if self.logits_lm is not self.logits:  # the padded columns dropped
+            self.logits.copy_(self.logits_lm[:, :V])
         if self.sampler is not None:
             src = self.logits
             if self.world > 1:  # all-gather the shards into the whole row on every rank

@@ -209,15 +209,19 @@ def _reference_step(dec, ids, caches, pos):
         a = f16(torch.nn.functional.silu(gu[:, :F]) * gu[:, F:])
         x = x + f16(a @ deq(lw["wd"], F, D))
     h = rms(x, dec.final_norm.cpu())
-    return f16(h @ deq(dec.lm_head, D, V))
+    return f16(h @ deq(dec.lm_head, D, dec.lm_cols)[:, :V])  # without the LM head's zero padding
 
 
-def test_decoder_steps_match_fp32_reference(cuda):
+@pytest.mark.parametrize("vocab", [1000, 1152])
+def test_decoder_steps_match_fp32_reference(cuda, vocab):
+    """vocab = 1152 (9 x 128 columns): the LM head runs padded to 1280 columns of
+    256-wide strips and its logits are copied back to 1152."""
     import torch
     from moat_b200.decode import DecoderConfig, Int4Decoder
-    cfg = DecoderConfig(layers=2, hidden=256, heads=2, head_dim=128, ffn=512, vocab=1000, max_len=48)
+    cfg = DecoderConfig(layers=2, hidden=256, heads=2, head_dim=128, ffn=512, vocab=vocab, max_len=48)
     N = 4
     dec = Int4Decoder(cfg, N, device=cuda, seed=3)
+    assert dec.lm_cols == (1280 if vocab == 1152 else vocab)
     dec.fill_prompt_cache(10, seed=4)
     caches = [(k.cpu().float().clone(), v.cpu().float().clone()) for k, v in zip(dec.k_cache, dec.v_cache)]
     ids = torch.tensor([1, 500, 999, 42], dtype=torch.int32, device=cuda)
