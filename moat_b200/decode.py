@@ -95,6 +95,14 @@ def tp_shards(cfg: DecoderConfig, world: int):
     return {"heads": head_bounds(cfg.heads, world), "ffn": cols(cfg.ffn), "vocab": cols(cfg.vocab)}
 
 
+def lm_head_cols(vocab_range: int) -> int:
+    """Stored width of an LM-head vocabulary range: a range of an odd number of
+    128-column blocks gets 128 zero-weight columns, so that its GEMM runs in 256-column
+    strips (a 128-wide strip takes a wave as long as a 256-wide one, so the wider strip
+    halves the waves); any other range is stored as it is."""
+    return vocab_range + 128 if vocab_range % 256 == 128 else vocab_range
+
+
 class Int4Decoder:
     """Random-init INT4 decoder for N traces decoding in lockstep, on one GPU or
     tensor-parallel over ``world`` GPUs (this process being ``rank``)."""
@@ -159,11 +167,9 @@ class Int4Decoder:
                 "ffn_norm": (1.0 + 0.02 * t.randn((D,), generator=g, device=self.dev)).float(),
             })
         self.final_norm = (1.0 + 0.02 * t.randn((D,), generator=g, device=self.dev)).float()
-        # The LM head streams in 256-column strips: a vocabulary range of an odd number of
-        # 128-column blocks (151,936 = 1187 x 128) gets 128 zero-weight columns, which
-        # halves the GEMM's waves (a 128-wide strip takes a wave as long as a 256-wide
-        # one); its logits are copied back to the range's own width.
-        self.lm_cols = Vl + 128 if Vl % 256 == 128 else Vl
+        # the LM head in 256-column strips (151,936 = 1187 x 128 -> 152,064 columns); its
+        # logits are copied back to the range's own width
+        self.lm_cols = lm_head_cols(Vl)
         self.lm_head = int4(D, V, cols=[(v0, v1)], pad=self.lm_cols - Vl)
         self.embed = (t.randn((V, D), generator=g, device=self.dev) * std).half()
         self.cs = rope_table(dh, cfg.max_len, cfg.theta).to(self.dev)

@@ -7,6 +7,8 @@
 * The Megatron split of config 5 over 1/2/4/8 ranks: head, FFN and vocabulary ranges
   cover their dimension, are whole 128-column units, and give every rank's GEMMs
   widths the fast kernel plan takes.
+* The LM head's zero-column padding (to whole 256-column strips) leaves the INT4 codes
+  and scales of the real columns bit for bit as they were (oracle quantizer).
 """
 
 import os
@@ -131,3 +133,23 @@ def test_small_vocab_split_falls_back_to_groups():
     sh = tp_shards(DecoderConfig(vocab=1056, ffn=512), 2)
     assert sh["vocab"] == [(0, 544), (544, 1056)]
     assert sh["ffn"] == [(0, 256), (256, 512)]
+
+
+def test_lm_head_padding_keeps_codes_and_scales():
+    from moat_b200.decode import DecoderConfig, lm_head_cols, tp_shards
+    from oracle import int4 as O
+    cfg = DecoderConfig()
+    for world in (1, 2, 4, 8):
+        for c0, c1 in tp_shards(cfg, world)["vocab"]:
+            cols = lm_head_cols(c1 - c0)
+            assert cols % 256 == 0 or (c1 - c0) % 256 != 128
+            assert cols - (c1 - c0) in (0, 128)
+    assert lm_head_cols(151936) == 152064 and lm_head_cols(76032) == 76032 and lm_head_cols(1000) == 1000
+    K, V = 64, 1152  # 9 x 128 columns -> 1280
+    w = O.make_weights(K, V, 31)
+    Vp = lm_head_cols(V)
+    wp = np.concatenate([w, np.zeros((K, Vp - V), np.float32)], axis=1)
+    plain = O.unpack_superblock_weights(O.quantize_pack_matrix(w)).reshape(K, V)
+    padded = O.unpack_superblock_weights(O.quantize_pack_matrix(wp)).reshape(K, Vp)
+    np.testing.assert_array_equal(padded[:, :V].view(np.uint16), plain.view(np.uint16))
+    assert not np.any(padded[:, V:])
